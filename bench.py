@@ -1,0 +1,444 @@
+"""Benchmark: π0.5 action chunks (prefill of 968 prefix tokens + 10 denoise steps, batch 1).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--batch B]
+
+One process per GPU (torchrun for N > 1). Every rank holds a full replica of the fp16 model
+(random N(0, 0.02) weights, seeded) and runs its own independent requests; there is no
+collective on the data path (the only collectives are the timing barrier and the max over
+ranks). One step = one action chunk per request: ``prefill`` (18 prefix-expert layers over
+968 tokens, writing the per-layer K/V cache) + ``denoise_loop_kv`` (10 Euler steps of the
+action expert, replayed as one CUDA graph), inputs resident in HBM. ``e2e`` times the public
+API ``PiZeroRunner.sample_graph`` from pinned host buffers (prefix embeddings and noise up,
+actions down) over the same steps.
+
+Prints one JSON line on rank 0 (schema in the project's build notes): value = chunks/s over all
+GPUs, ms_per_step = ms per chunk (per GPU), roofline of the dominant kernel family measured
+live with CUDA events, the CPU oracle timed on a bounded sample as ``cpu_baseline``, SM clocks
+sampled during the timed region, and the number of library kernels launched.
+
+``--impl reference`` times the reference's CPU implementation of the path — the numpy oracle
+that restates it (the reference itself needs TVM, absent here) — on the host cores, on a
+bounded sample per step, and prints the same line with ``"impl": "reference"``.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for _p in (ROOT, os.path.join(ROOT, "mlc-vla_b200")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import numpy as np  # noqa: E402
+
+METRIC = "pi0.5 ms/action-chunk (prefill968+10 steps, bs1); chunks/s at 1/2/4/8 GPU"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return d, "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def full_config():
+    from mlc_vla.model.pi0 import Pi0Config
+
+    return Pi0Config(action_horizon=50, action_dim=32, num_denoise_steps=10, dtype="float16")
+
+
+# ------------------------------------------------------------------------------------------
+# algorithmic work per kernel family (per chunk), for the roofline
+# ------------------------------------------------------------------------------------------
+def work_model(cfg, batch):
+    """family -> (work per chunk, unit, bound). FLOPs for the compute-bound prefill, HBM bytes
+    (weights + K/V + activations, each read or written once) for the weight-bound denoise."""
+    vlm, ae = cfg.vlm, cfg.action_expert
+    L, H, KV, hd = vlm.depth, vlm.num_heads, vlm.num_kv_heads, vlm.head_dim
+    hq, hkv = H * hd, KV * hd
+    W0, F0, W1, F1 = vlm.width, vlm.mlp_dim, ae.width, ae.mlp_dim
+    P, S, D, N = cfg.prefix_len, cfg.suffix_len, cfg.action_dim, cfg.num_denoise_steps
+    M0, M1 = batch * P, batch * S
+    e = 2
+    w = {}
+    w["prefill.qkv_rope_gemm"] = (2 * M0 * W0 * ((L - 1) * (hq + 2 * hkv) + 2 * hkv), "flop", "tensor")
+    w["prefill.attention"] = ((L - 1) * 4 * batch * H * P * P * hd, "flop", "tensor")
+    w["prefill.o_gemm"] = ((L - 1) * 2 * M0 * W0 * hq, "flop", "tensor")
+    w["prefill.gate_up_geglu_gemm"] = ((L - 1) * 2 * M0 * W0 * 2 * F0, "flop", "tensor")
+    w["prefill.down_gemm"] = ((L - 1) * 2 * M0 * W0 * F0, "flop", "tensor")
+    w["prefill.rmsnorm"] = ((2 * L - 1) * 2 * M0 * W0 * e, "byte", "hbm")
+    nmod = (2 * L + 1) * 3 * W1
+    w["denoise.time_mlp_modulation_gemv"] = ((2 * W1 * W1 + nmod * W1) * e, "byte", "hbm")
+    per_step = {
+        "denoise.qkv_rope_gemm": L * ((hq + 2 * hkv) * W1 * e + M1 * (W1 * e + hq * 4 + 2 * hkv * 4)),
+        "denoise.attention": L * batch * KV * (P + S) * hd * (4 + e),
+        "denoise.o_gemm": L * (W1 * hq * e + M1 * (hq + 2 * W1) * e),
+        "denoise.gate_up_geglu_gemm": L * (2 * F1 * W1 * e + M1 * (W1 + F1) * e),
+        "denoise.down_gemm": L * (W1 * F1 * e + M1 * (F1 + 2 * W1) * e),
+        "denoise.ada_rmsnorm": (2 * L + 1) * 2 * M1 * W1 * e,
+        "denoise.action_in": (W1 * D + M1 * W1) * e,
+        "denoise.action_out_euler": (W1 * D) * e + M1 * W1 * e,
+    }
+    for k, v in per_step.items():
+        w[k] = (N * v, "byte", "hbm")
+    return w
+
+
+# ------------------------------------------------------------------------------------------
+# clocks sampled during the timed region
+# ------------------------------------------------------------------------------------------
+class ClockSampler:
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_gpu{gpu_index}.csv")
+
+    def __enter__(self):
+        try:
+            os.makedirs(os.path.dirname(self.path), exist_ok=True)
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self):
+        if self.proc is None or not os.path.exists(self.path):
+            return None
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------------------------------------
+# CPU baseline: the oracle on a bounded sample
+# ------------------------------------------------------------------------------------------
+def cpu_sample_chunk_ms(reps=1):
+    """Time the numpy oracle on a 2-layer model with every π0.5 width (prefill of 968 tokens and
+    one denoise step of 50 tokens) and scale to the 18-layer chunk:
+    prefill_18 ≈ 17 · t_prefill(2 layers: one full layer + the last layer's k/v), and
+    step_18 ≈ 9 · t_step(2 layers); chunk = prefill_18 + 10 · step_18."""
+    import torch
+
+    from mlc_vla.model.pi0 import Pi0Config
+    from mlc_vla.model.pi0.pi0_model import backbone_named_params
+    from oracle import pi0_oracle as O
+
+    cfg = Pi0Config(paligemma_variant="gemma_2b_2l", action_expert_variant="gemma_300m_2l",
+                    action_horizon=50, action_dim=32, num_denoise_steps=10, dtype="float16")
+    g = torch.Generator().manual_seed(0)
+    raw = {n: (0.02 * torch.randn(s.shape, generator=g)).numpy() for n, s in backbone_named_params(cfg)}
+    p = O.prepare_params(raw, "float16")
+    rng = np.random.default_rng(1)
+    prefix = rng.standard_normal((1, cfg.prefix_len, cfg.vlm.width)).astype(np.float32)
+    x_t = rng.standard_normal((1, 50, 32)).astype(np.float32)
+    te = O.sinusoidal_time_emb(1.0, cfg.action_expert.width)
+    pm = O.prefix_mask(cfg.prefix_len)
+    sc, ss = O.suffix_rope(cfg, cfg.prefix_len)
+    tp, ts = [], []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        k, v = O.prefill(p, cfg, prefix, pm)
+        t1 = time.perf_counter()
+        O.denoise_step_kv(p, cfg, k, v, x_t, te, sc, ss, pm)
+        t2 = time.perf_counter()
+        tp.append(t1 - t0)
+        ts.append(t2 - t1)
+    tpre, tstep = float(np.median(tp)), float(np.median(ts))
+    chunk_ms = (17 * tpre + 10 * 9 * tstep) * 1e3
+    return chunk_ms, {"prefill_2layers_ms": tpre * 1e3, "step_2layers_ms": tstep * 1e3}
+
+
+def blas_threads():
+    try:
+        from threadpoolctl import threadpool_info
+
+        n = [i.get("num_threads", 0) for i in threadpool_info() if i.get("user_api") == "blas"]
+        return max(n) if n else os.cpu_count()
+    except Exception:  # noqa: BLE001
+        return os.cpu_count()
+
+
+CPU_SAMPLE = ("numpy oracle (fp32 BLAS, fp16 rounding emulated) on a 2-layer model with every "
+              "pi0.5 width: prefill of 968 tokens + one 50-token denoise step, scaled to 18 layers "
+              "and 10 steps (17 x prefill + 90 x step)")
+
+
+# ------------------------------------------------------------------------------------------
+# reference arm
+# ------------------------------------------------------------------------------------------
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    cores = blas_threads()
+    for _ in range(args.warmup):
+        cpu_sample_chunk_ms()
+    t = []
+    for _ in range(args.steps):
+        ms, _ = cpu_sample_chunk_ms()
+        t.append(ms)
+    ms = float(np.mean(t))
+    value = 1000.0 / ms
+    line = {
+        "metric": METRIC, "value": value, "unit": "chunks/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+        "impl": "reference",
+        "config": {"workload": "pi0.5 fp16 bs1: prefill(968) + 10 Euler steps (host CPU)",
+                   "global_batch": 1, "seq_len": 968, "parallelism": "cpu"},
+        "cpu_baseline": {"value": value, "unit": "chunks/s", "cores": cores, "kind": "port",
+                         "sample": CPU_SAMPLE},
+        "e2e": {"value": value, "unit": "chunks/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------------------------------------
+# B200 arm
+# ------------------------------------------------------------------------------------------
+def make_weights(named_params, device, seed=0):
+    import torch
+
+    g = torch.Generator(device=device).manual_seed(seed)
+    out = []
+    for _, spec in named_params:
+        t = torch.randn(spec.shape, generator=g, device=device, dtype=torch.float32).mul_(0.02)
+        out.append(t.to(torch.float16))
+    return out
+
+
+def run_b200(args):
+    import torch
+    import torch.distributed as dist
+
+    from mlc_vla import _lib
+    from mlc_vla.sample import PiZeroRunner, make_prefix_mask_np, make_rope_np, make_time_embs
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    cfg = full_config()
+    B = args.batch
+    runner = PiZeroRunner(cfg, target="cuda", max_batch=B, device=local)
+    rt = runner.ex
+    params = make_weights(rt.named_params, dev, seed=0)
+    rt.bind(params)
+    lib = _lib.load()
+
+    # device-resident inputs (per-rank seeds: independent requests)
+    gen = torch.Generator(device=dev).manual_seed(1000 + rank)
+    P, S, D, W0 = cfg.prefix_len, cfg.suffix_len, cfg.action_dim, cfg.vlm.width
+    prefix = torch.randn((B, P, W0), generator=gen, device=dev).to(torch.float16)
+    noise = torch.randn((B, S, D), generator=gen, device=dev)
+    pm = torch.from_numpy(np.concatenate([make_prefix_mask_np(P)] * B, 0)).to(dev)
+    c, s = make_rope_np(S, cfg.vlm.head_dim, cfg.rope_theta, offset=P)
+    sc = torch.from_numpy(np.concatenate([c] * B, 0)).to(dev)
+    ss = torch.from_numpy(np.concatenate([s] * B, 0)).to(dev)
+    te = torch.from_numpy(np.concatenate(make_time_embs(cfg.num_denoise_steps, cfg.action_expert.width), 0)).to(dev, torch.float16)
+    vlm = cfg.vlm
+    kv_shape = (vlm.depth, B, vlm.num_kv_heads, P, vlm.head_dim)
+    keys = torch.empty(kv_shape, dtype=torch.float32, device=dev)
+    values = torch.empty(kv_shape, dtype=torch.float16, device=dev)
+    x = torch.empty((B, S, D), dtype=torch.float32, device=dev)
+
+    def chunk():
+        rt.prefill(prefix, pm, keys=keys, values=values)
+        rt.denoise_loop_kv(keys, values, noise, te, sc, ss, pm, out=x)
+
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(args.warmup):
+        chunk()
+    torch.cuda.synchronize(dev)
+
+    # per-kernel-family device times (profiled pass, eager launches bracketed by events)
+    lib.pi0_profile_enable(rt._ctx, 1)
+    chunk()
+    torch.cuda.synchronize(dev)
+    nf = lib.pi0_profile_families()
+    import ctypes
+
+    launches = (ctypes.c_int64 * nf)()
+    total = (ctypes.c_double * nf)()
+    _lib.check(lib.pi0_profile_read(rt._ctx, nf, launches, total), rt._ctx)
+    lib.pi0_profile_enable(rt._ctx, 0)
+    fam = {lib.pi0_profile_family_name(i).decode(): (int(launches[i]), float(total[i]))
+           for i in range(nf) if launches[i]}
+    for _ in range(2):
+        chunk()  # re-warm the graph path
+    torch.cuda.synchronize(dev)
+
+    # timed region (device-resident inputs)
+    barrier()
+    torch.cuda.synchronize(dev)
+    n0 = lib.pi0_launch_count(rt._ctx)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        e0.record(stream)
+        for _ in range(args.steps):
+            chunk()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+    n_launch = lib.pi0_launch_count(rt._ctx) - n0
+    elapsed = e0.elapsed_time(e1)
+    barrier()
+    t = torch.tensor([elapsed], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    elapsed_max = float(t.item())
+    ms_chunk = elapsed_max / args.steps
+    value = world * B * args.steps / (elapsed_max / 1e3)
+
+    # end to end through the public API: pinned host prefix + noise up, actions down
+    e2e = None
+    if not args.no_e2e:
+        host_prefix = prefix.cpu().pin_memory()
+        host_noise = noise.cpu().numpy()
+        for _ in range(max(1, args.warmup)):
+            runner.sample_graph(params, host_prefix, noise=host_noise)
+        torch.cuda.synchronize(dev)
+        barrier()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record(stream)
+        for _ in range(args.steps):
+            runner.sample_graph(params, host_prefix, noise=host_noise)
+        f1.record(stream)
+        torch.cuda.synchronize(dev)
+        te2e = torch.tensor([f0.elapsed_time(f1)], device=dev)
+        if world > 1:
+            dist.all_reduce(te2e, op=dist.ReduceOp.MAX)
+        h2d = (host_prefix.numel() * host_prefix.element_size() + host_noise.nbytes
+               + B * P * 4 + 2 * B * S * (cfg.vlm.head_dim // 2) * 4
+               + cfg.num_denoise_steps * cfg.action_expert.width * 2)
+        e2e = {"value": world * B * args.steps / (float(te2e.item()) / 1e3), "unit": "chunks/s",
+               "ms_per_step": float(te2e.item()) / args.steps,
+               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(B * S * D * 4)}
+
+    # roofline of the dominant kernel family
+    pk, pk_kind = peaks()
+    wm = work_model(cfg, B)
+    dom = max(fam, key=lambda k: fam[k][1])
+    work, unit, bound = wm.get(dom, (0, "byte", "hbm"))
+    ms = fam[dom][1]
+    if bound == "tensor":
+        achieved = work / (ms / 1e3) / 1e12
+        peak = pk.get("bf16_tflops_sustained", pk.get("bf16_tflops"))
+        runit = "TFLOP/s"
+    else:
+        achieved = work / (ms / 1e3) / 1e9
+        peak = pk["hbm_gbs"]
+        runit = "GB/s"
+    families = {}
+    for k, (n, tot) in sorted(fam.items(), key=lambda kv: -kv[1][1]):
+        wk = wm.get(k)
+        ent = {"launches": n, "ms": round(tot, 4), "share": round(tot / sum(v[1] for v in fam.values()), 4)}
+        if wk:
+            if wk[2] == "tensor":
+                ent["tflops"] = round(wk[0] / (tot / 1e3) / 1e12, 1)
+            else:
+                ent["gbs"] = round(wk[0] / (tot / 1e3) / 1e9, 1)
+        families[k] = ent
+    roofline = {"bound": bound, "kernel": dom, "achieved": round(achieved, 2), "peak": peak,
+                "unit": runit, "frac": round(achieved / peak, 4), "traffic": None,
+                "peak_source": f"{pk_kind} ({'bf16_tflops_sustained' if bound == 'tensor' else 'hbm_gbs'})",
+                "work_per_launch": work / max(1, fam[dom][0]), "families": families}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cms, detail = cpu_sample_chunk_ms()
+        cpu = {"value": 1000.0 / cms, "unit": "chunks/s", "cores": blas_threads(), "kind": "port",
+               "sample": CPU_SAMPLE, **{k: round(v, 2) for k, v in detail.items()}}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "chunks/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_chunk,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic (random N(0,0.02) weights, N(0,1) prefix_embs and noise, seeded)",
+            "config": {"workload": "pi0.5 fp16, per GPU batch %d: prefill(968) + denoise_loop_kv "
+                                   "(10 Euler steps, one CUDA graph); horizon 50, action_dim 32" % B,
+                       "model": "pi0.5 (gemma_2b prefix expert + gemma_300m action expert)",
+                       "global_batch": world * B, "seq_len": P, "parallelism": f"dp{world} (replicas)",
+                       "l2": "inputs larger than L2 (4.8 GB of weights streamed per chunk)"},
+            "e2e": e2e, "roofline": roofline, "cpu_baseline": cpu, "clocks": clk.summary(),
+            "gpu_launches": int(n_launch),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    rt.close()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_b200(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

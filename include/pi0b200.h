@@ -1,0 +1,140 @@
+/*
+ * pi0b200.h — C ABI of libpi0b200.so, the B200 (sm_100a) π0.5 M1 hot path.
+ *
+ * The reference compiles the π0.5 backbone with TVM and calls three exported functions
+ * through a Relax VM, passing the packed parameter list as the last argument:
+ *
+ *   vm["prefill"](prefix_embs, prefix_mask, params)                -> (keys, values)
+ *   vm["denoise_step_kv"](keys, values, x_t, time_emb, suffix_cos,
+ *                         suffix_sin, prefix_mask, params)         -> v_t
+ *   vm["denoise_loop_kv"](keys, values, x0, time_embs, suffix_cos,
+ *                         suffix_sin, prefix_mask, params)         -> x
+ *
+ * (python/mlc_vla/model/pi0/pi0_model.py:128-194, spec :197-255; called from
+ * python/mlc_vla/sample.py:128,158,184). This header is the C-level replacement of that
+ * VM boundary: plain device pointers and sizes, one context per (GPU, host thread), every
+ * call asynchronous on the caller's stream and returning a status code.
+ *
+ * Tensor layouts (row-major, batch B ≤ cfg.max_batch; the reference fixes B = 1):
+ *   prefix_embs  [B, P, W0]            model dtype
+ *   prefix_mask  [B, P]                fp32 additive (0 = valid, -1e9 = padding)
+ *   keys         [L, B, KV, P, hd]     fp32 (post-RoPE)
+ *   values       [L, B, KV, P, hd]     model dtype
+ *   x_t          [B, S, D]             model dtype
+ *   x0, x, v     [B, S, D]             fp32
+ *   time_emb     [1, W1]               model dtype (shared by the batch)
+ *   time_embs    [N, W1]               model dtype
+ *   suffix_cos/sin [B, S, hd/2]        fp32 (per-request RoPE offset = #valid prefix)
+ * where P = prefix_len, S = action_horizon, D = action_dim, W0/W1 = expert widths,
+ * L = depth, KV = num_kv_heads, hd = head_dim, N = num_denoise_steps.
+ */
+#ifndef PI0B200_H_
+#define PI0B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* pi0_stream_t; /* the same type as cudaStream_t */
+typedef struct pi0_ctx pi0_ctx;
+
+enum pi0_status {
+  PI0_OK = 0,
+  PI0_ERR_INVALID = 1,     /* bad argument, shape or configuration */
+  PI0_ERR_CUDA = 2,        /* a CUDA runtime call failed */
+  PI0_ERR_NO_PARAMS = 3,   /* compute called before pi0_set_params */
+  PI0_ERR_DEVICE = 4,      /* a kernel reported an error flag (bounded wait gave up) */
+  PI0_ERR_UNSUPPORTED = 5  /* configuration this build does not implement */
+};
+
+enum pi0_dtype { PI0_F16 = 0, PI0_BF16 = 1, PI0_F32 = 2, PI0_U32 = 3 };
+
+/* Weight formats: the reference's quantisation presets (python/mlc_vla/quant.py:370-387). */
+enum pi0_quant { PI0_QUANT_NONE = 0, PI0_QUANT_Q4 = 1 /* q4f16_1 / q4bf16_1 */,
+                 PI0_QUANT_Q3 = 2 /* q3f16_1 */ };
+
+/* Model shape: the fields of Pi0Config / GemmaExpertConfig the backbone build reads
+ * (python/mlc_vla/model/pi0/pi0_config.py:17-170). */
+typedef struct pi0_config {
+  int32_t vlm_width, vlm_mlp_dim;     /* W0, F0 */
+  int32_t ae_width, ae_mlp_dim;       /* W1, F1 */
+  int32_t depth, num_heads, num_kv_heads, head_dim;
+  int32_t prefix_len, action_horizon, action_dim;
+  int32_t num_denoise_steps;
+  int32_t dtype;                      /* pi0_dtype: PI0_F16 or PI0_BF16 */
+  int32_t quant;                      /* pi0_quant */
+  int32_t max_batch;                  /* workspace sizing; calls may use any B ≤ this */
+  float rms_norm_eps;                 /* 1e-6 */
+  float rope_theta;                   /* 1e4 */
+} pi0_config;
+
+/* Replaces compile_model + relax.VirtualMachine (python/mlc_vla/sample.py:91-95,
+ * compile.py:99-133): allocates the context, workspaces and the packed-weight arena on
+ * `device`. */
+int pi0_create(const pi0_config* cfg, int device, pi0_ctx** out);
+int pi0_destroy(pi0_ctx* ctx);
+/* Text of the last error on this context (valid until the next call on it). */
+const char* pi0_last_error(const pi0_ctx* ctx);
+
+/* The packed-parameter table, in the reference's export order (export_tvm named_params,
+ * python/mlc_vla/compile.py:34-38): name, shape (ndim ≤ 2) and pi0_dtype of entry i. */
+int pi0_num_params(const pi0_ctx* ctx);
+int pi0_param_info(const pi0_ctx* ctx, int i, const char** name, int* ndim, int64_t shape[2],
+                   int* dtype);
+
+/* Replaces the per-call `params` argument of every VM function (sample.py:98-100,128): takes
+ * the device pointers of all n = pi0_num_params() parameters, in table order, and repacks
+ * them into the context's weight arena (the caller keeps ownership of its buffers). */
+int pi0_set_params(pi0_ctx* ctx, const void* const* params, int n, pi0_stream_t stream);
+
+/* vm["prefill"] (pi0_model.py:128-140): writes keys and values for B requests. */
+int pi0_prefill(pi0_ctx* ctx, int batch, const void* prefix_embs, const float* prefix_mask,
+                float* keys, void* values, pi0_stream_t stream);
+
+/* vm["denoise_step_kv"] (pi0_model.py:142-163): one suffix-only step; v_out fp32. */
+int pi0_denoise_step_kv(pi0_ctx* ctx, int batch, const float* keys, const void* values,
+                        const void* x_t, const void* time_emb, const float* suffix_cos,
+                        const float* suffix_sin, const float* prefix_mask, float* v_out,
+                        pi0_stream_t stream);
+
+/* vm["denoise_loop_kv"] (pi0_model.py:165-194): cfg.num_denoise_steps Euler steps
+ * (dt = -1/N, x in fp32), replayed as one CUDA graph per distinct argument set. x_out may
+ * alias x0. */
+int pi0_denoise_loop_kv(pi0_ctx* ctx, int batch, const float* keys, const void* values,
+                        const float* x0, const void* time_embs, const float* suffix_cos,
+                        const float* suffix_sin, const float* prefix_mask, float* x_out,
+                        pi0_stream_t stream);
+
+/* Replaces GroupQuantize.quantize_weight (python/mlc_vla/quant.py:195-266) on the GPU:
+ * w [n_out, k] model dtype -> q_weight [n_out, ceil(k/G)*G/epw] uint32 and
+ * q_scale [n_out, ceil(k/G)] model dtype, for quant PI0_QUANT_Q4 (G=32, 8 codes per word)
+ * or PI0_QUANT_Q3 (G=40, 10 codes per word). Context-free. */
+int pi0_quantize_weight(int quant, int dtype, const void* w, int64_t n_out, int64_t k,
+                        uint32_t* q_weight, void* q_scale, pi0_stream_t stream);
+
+/* The inverse (quant.py:176-193): w = (code - max_int) * scale in the model dtype. */
+int pi0_dequantize_weight(int quant, int dtype, const uint32_t* q_weight, const void* q_scale,
+                          int64_t n_out, int64_t k, void* w, pi0_stream_t stream);
+
+/* ---- measurement hooks (no counterpart in the reference; used by bench.py) -------------- */
+
+/* Kernels this context has launched so far (a replayed graph counts its kernel nodes). */
+int64_t pi0_launch_count(const pi0_ctx* ctx);
+
+/* While enabled, every kernel launch is bracketed by CUDA events on its stream and
+ * denoise_loop_kv runs without graph capture, so per-kernel-family device times can be read
+ * back. Enabling clears earlier records. */
+int pi0_profile_enable(pi0_ctx* ctx, int on);
+/* Synchronises the recorded events and returns, per kernel family (index < pi0_profile_families),
+ * its launch count and total device milliseconds. */
+int pi0_profile_read(pi0_ctx* ctx, int n_families, int64_t* launches, double* total_ms);
+int pi0_profile_families(void);
+const char* pi0_profile_family_name(int family);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* PI0B200_H_ */

@@ -1,0 +1,287 @@
+// Tiled GEMM  C[M,N] = A[M,K] · W[N,K]^T  (A and W row-major, K contiguous — the reference's
+// nn.Linear layout [out, in]) on warp-level mma.sync tensor cores, fp32 accumulation, with the
+// epilogue fused: every Linear of the π0.5 backbone ends in one of the epilogue functors below
+// (RoPE + K/V-cache write for q/k/v, residual add, gated residual add, GeGLU).
+//
+// Split-K: gridDim.z > 1 splits K; every split writes its fp32 partial tile to a workspace and
+// the last split to arrive (atomic ticket per output tile) sums the partials in split order and
+// runs the epilogue, so results do not depend on arrival order. The ticket is reset by that
+// last split, so the same workspace is reusable (and CUDA-graph replayable) without clearing.
+#pragma once
+
+#include "common.cuh"
+
+namespace pi0 {
+
+template <typename T>
+struct GemmArgs {
+  const T* A;
+  int lda;
+  const T* W;
+  int ldw;
+  int M, N, K;
+  int k_split_len;   // K range of one split (multiple of 32)
+  float* ws;         // split-K partials [splits][M][N]
+  int* tickets;      // one int per output tile, zero between launches
+};
+
+// ---- epilogues: operator()(row, col, v(col), v(col+1)); col is even ----
+
+template <typename T>
+struct EpiStore {  // y = round(round(acc) + bias) (bias optional), stored in the model dtype
+  T* out;
+  int ldo;
+  const T* bias;
+  __device__ void operator()(int r, int c, float v0, float v1) const {
+    float a = Tr<T>::r(v0), b = Tr<T>::r(v1);
+    if (bias) {
+      a = a + Tr<T>::f(bias[c]);
+      b = b + Tr<T>::f(bias[c + 1]);
+    }
+    *reinterpret_cast<uint32_t*>(out + (size_t)r * ldo + c) = Tr<T>::pack(a, b);
+  }
+};
+
+template <typename T>
+struct EpiResid {  // prefix residual (gemma_dual.py:338,340): x = round(x + round(acc))
+  T* x;
+  int ldx;
+  __device__ void operator()(int r, int c, float v0, float v1) const {
+    T* p = x + (size_t)r * ldx + c;
+    float a = Tr<T>::f(p[0]) + Tr<T>::r(v0);
+    float b = Tr<T>::f(p[1]) + Tr<T>::r(v1);
+    *reinterpret_cast<uint32_t*>(p) = Tr<T>::pack(a, b);
+  }
+};
+
+template <typename T>
+struct EpiGatedResid {  // suffix residual (gemma_dual.py:91-94): x = round(x + round(round(acc)·gate))
+  T* x;
+  int ldx;
+  const T* gate;      // [rows_per_gate_group ...]: gate[(r / rows_per_gate) * gate_stride + c]
+  int rows_per_gate;  // rows that share one gate vector (S·B when the time is shared)
+  int gate_stride;
+  __device__ void operator()(int r, int c, float v0, float v1) const {
+    const T* g = gate + (size_t)(r / rows_per_gate) * gate_stride + c;
+    T* p = x + (size_t)r * ldx + c;
+    float a = Tr<T>::f(p[0]) + Tr<T>::r(Tr<T>::r(v0) * Tr<T>::f(g[0]));
+    float b = Tr<T>::f(p[1]) + Tr<T>::r(Tr<T>::r(v1) * Tr<T>::f(g[1]));
+    *reinterpret_cast<uint32_t*>(p) = Tr<T>::pack(a, b);
+  }
+};
+
+// GeGLU (gemma_dual.py:132-135) on interleaved gate/up weights: packed weight row 2j is gate
+// row j and row 2j+1 is up row j, so (col, col+1) = (gate_j, up_j).
+// h[r, j] = round(round(gelu_tanh(round(gate))) · round(up)).
+template <typename T>
+struct EpiGeglu {
+  T* h;
+  int ldh;
+  __device__ void operator()(int r, int c, float v0, float v1) const {
+    float g = Tr<T>::r(gelu_tanh_f(Tr<T>::r(v0)));
+    h[(size_t)r * ldh + (c >> 1)] = Tr<T>::t(g * Tr<T>::r(v1));
+  }
+};
+
+// q/k/v projection with RoPE and the K/V-cache write fused (gemma_dual.py:236-275).
+// Packed weight rows of the q and k blocks are permuted per head so that columns (2i, 2i+1)
+// hold original dims (i, i + hd/2); v rows keep their order.
+//   q  -> fp32 [rows, H, hd], rotated and scaled by hd^-0.5
+//   k  -> fp32 cache [B, KV, T, hd] at (b, kvh, pos), rotated
+//   v  -> model-dtype cache, same layout
+// Rows are r = b·T + pos. RoPE tables: cos/sin[(b·cs_bstride) + pos·(hd/2) + i] fp32.
+template <typename T>
+struct EpiQkvRope {
+  float* q;
+  float* k;
+  T* v;
+  const float* cos;
+  const float* sin;
+  int cs_bstride;
+  int T_len;     // positions per request
+  int H, KV, hd;
+  int col0;      // global column offset of this launch (skip q rows for the last prefill layer)
+  float qscale;
+  __device__ void operator()(int r, int c_local, float v0, float v1) const {
+    int c = c_local + col0;
+    int hq = H * hd, hkv = KV * hd;
+    int b = r / T_len, pos = r - b * T_len;
+    if (c < hq + hkv) {
+      bool isq = c < hq;
+      int cc = isq ? c : c - hq;
+      int head = cc / hd, i = (cc - head * hd) >> 1, half = hd >> 1;
+      size_t t = (size_t)b * cs_bstride + (size_t)pos * half + i;
+      float cs = cos[t], sn = sin[t];
+      float x1 = Tr<T>::r(v0), x2 = Tr<T>::r(v1);
+      float o1 = __fsub_rn(__fmul_rn(x1, cs), __fmul_rn(x2, sn));
+      float o2 = __fadd_rn(__fmul_rn(x2, cs), __fmul_rn(x1, sn));
+      if (isq) {
+        float* p = q + ((size_t)r * H + head) * hd;
+        p[i] = __fmul_rn(o1, qscale);
+        p[i + half] = __fmul_rn(o2, qscale);
+      } else {
+        float* p = k + (((size_t)b * KV + head) * T_len + pos) * hd;
+        p[i] = o1;
+        p[i + half] = o2;
+      }
+    } else {
+      int cc = c - hq - hkv;
+      int head = cc / hd, d = cc - head * hd;
+      T* p = v + (((size_t)b * KV + head) * T_len + pos) * hd + d;
+      *reinterpret_cast<uint32_t*>(p) = Tr<T>::pack(v0, v1);
+    }
+  }
+};
+
+// ---- kernel ----
+template <typename T, int BM, int BN, int WM, int WN, int STAGES>
+struct GemmCfg {
+  static constexpr int BK = 32;
+  static constexpr int LDS = BK + 8;  // halves per smem row (80 B: conflict-free ldmatrix)
+  static constexpr int WARPS_M = BM / WM, WARPS_N = BN / WN;
+  static constexpr int NT = WARPS_M * WARPS_N * 32;
+  static constexpr int MI = WM / 16, NI = WN / 8;
+  static constexpr int SMEM = STAGES * (BM + BN) * LDS * 2;
+};
+
+template <typename T, int BM, int BN, int WM, int WN, int STAGES, class Epi>
+__global__ void __launch_bounds__(GemmCfg<T, BM, BN, WM, WN, STAGES>::NT)
+    gemm_mma_kernel(GemmArgs<T> g, Epi epi) {
+  using C = GemmCfg<T, BM, BN, WM, WN, STAGES>;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  T* sA = reinterpret_cast<T*>(smem_raw);
+  T* sB = sA + STAGES * BM * C::LDS;
+  __shared__ int s_last;
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int wm = warp / C::WARPS_N, wn = warp % C::WARPS_N;
+  const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+  const int kbeg = blockIdx.z * g.k_split_len;
+  const int kend = min(g.K, kbeg + g.k_split_len);
+  const int nk = (kend - kbeg) / C::BK;
+
+  auto load_stage = [&](int stage, int kt) {
+    const int k0 = kbeg + kt * C::BK;
+    T* a = sA + stage * BM * C::LDS;
+    T* b = sB + stage * BN * C::LDS;
+    for (int i = tid; i < BM * 4; i += C::NT) {
+      int row = i >> 2, ch = i & 3;
+      int gr = m0 + row;
+      const T* src = g.A + (size_t)min(gr, g.M - 1) * g.lda + k0 + ch * 8;
+      cp_async16(a + row * C::LDS + ch * 8, src, gr < g.M ? 16 : 0);
+    }
+    for (int i = tid; i < BN * 4; i += C::NT) {
+      int row = i >> 2, ch = i & 3;
+      int gr = n0 + row;
+      const T* src = g.W + (size_t)min(gr, g.N - 1) * g.ldw + k0 + ch * 8;
+      cp_async16(b + row * C::LDS + ch * 8, src, gr < g.N ? 16 : 0);
+    }
+  };
+
+  float acc[C::MI][C::NI][4];
+#pragma unroll
+  for (int i = 0; i < C::MI; ++i)
+#pragma unroll
+    for (int j = 0; j < C::NI; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[i][j][e] = 0.f;
+
+#pragma unroll
+  for (int s = 0; s < STAGES - 1; ++s) {
+    if (s < nk) load_stage(s, s);
+    cp_async_commit();
+  }
+
+  for (int kt = 0; kt < nk; ++kt) {
+    cp_async_wait<STAGES - 2>();
+    __syncthreads();
+    {
+      int nxt = kt + STAGES - 1;
+      if (nxt < nk) load_stage(nxt % STAGES, nxt);
+      cp_async_commit();
+    }
+    const T* a = sA + (kt % STAGES) * BM * C::LDS;
+    const T* b = sB + (kt % STAGES) * BN * C::LDS;
+#pragma unroll
+    for (int ks = 0; ks < C::BK; ks += 16) {
+      uint32_t af[C::MI][4], bf[C::NI][2];
+#pragma unroll
+      for (int i = 0; i < C::MI; ++i) {
+        const T* p = a + (wm * WM + i * 16 + (lane & 15)) * C::LDS + ks + (lane >> 4) * 8;
+        ldsm_x4(af[i][0], af[i][1], af[i][2], af[i][3], p);
+      }
+#pragma unroll
+      for (int j = 0; j < C::NI; j += 2) {
+        const T* p = b + (wn * WN + j * 8 + (lane & 7) + ((lane >> 4) << 3)) * C::LDS + ks +
+                     ((lane >> 3) & 1) * 8;
+        ldsm_x4(bf[j][0], bf[j][1], bf[j + 1][0], bf[j + 1][1], p);
+      }
+#pragma unroll
+      for (int i = 0; i < C::MI; ++i)
+#pragma unroll
+        for (int j = 0; j < C::NI; ++j) mma16816<T>(acc[i][j], af[i], bf[j]);
+    }
+  }
+  cp_async_wait<0>();
+
+  const int gq = lane >> 2, tq = lane & 3;
+  if (gridDim.z > 1) {
+    // deterministic split-K fix-up
+    float* part = g.ws + (size_t)blockIdx.z * g.M * g.N;
+#pragma unroll
+    for (int i = 0; i < C::MI; ++i)
+#pragma unroll
+      for (int j = 0; j < C::NI; ++j)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          int r = m0 + wm * WM + i * 16 + gq + h * 8;
+          int c = n0 + wn * WN + j * 8 + tq * 2;
+          if (r < g.M && c < g.N)
+            *reinterpret_cast<float2*>(part + (size_t)r * g.N + c) =
+                make_float2(acc[i][j][2 * h], acc[i][j][2 * h + 1]);
+        }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+      int* t = g.tickets + blockIdx.y * gridDim.x + blockIdx.x;
+      int prev = atomicAdd(t, 1);
+      s_last = (prev == (int)gridDim.z - 1);
+      if (s_last) *t = 0;
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+#pragma unroll
+    for (int i = 0; i < C::MI; ++i)
+#pragma unroll
+      for (int j = 0; j < C::NI; ++j)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          int r = m0 + wm * WM + i * 16 + gq + h * 8;
+          int c = n0 + wn * WN + j * 8 + tq * 2;
+          if (r < g.M && c < g.N) {
+            float s0 = 0.f, s1 = 0.f;
+            for (int z = 0; z < (int)gridDim.z; ++z) {
+              float2 v = __ldcg(reinterpret_cast<const float2*>(g.ws + (size_t)z * g.M * g.N +
+                                                               (size_t)r * g.N + c));
+              s0 += v.x;
+              s1 += v.y;
+            }
+            epi(r, c, s0, s1);
+          }
+        }
+    return;
+  }
+#pragma unroll
+  for (int i = 0; i < C::MI; ++i)
+#pragma unroll
+    for (int j = 0; j < C::NI; ++j)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        int r = m0 + wm * WM + i * 16 + gq + h * 8;
+        int c = n0 + wn * WN + j * 8 + tq * 2;
+        if (r < g.M && c < g.N) epi(r, c, acc[i][j][2 * h], acc[i][j][2 * h + 1]);
+      }
+}
+
+}  // namespace pi0

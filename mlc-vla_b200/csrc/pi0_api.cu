@@ -1,0 +1,1047 @@
+// libpi0b200.so — context, parameter table, weight arena and the three exported functions of
+// the π0.5 M1 hot path (prefill, denoise_step_kv, denoise_loop_kv) behind the C ABI declared in
+// include/pi0b200.h.
+//
+// One context owns, on one GPU:
+//   * the parameter table in the reference's export order (names, shapes, dtypes);
+//   * a weight arena holding a repacked copy of the caller's parameters: per layer the q/k/v
+//     rows of each expert are concatenated (q and k rows permuted per head for the RoPE
+//     epilogue), gate/up rows are interleaved for the GeGLU epilogue, and the 2·L+1 adaRMS
+//     modulation matrices of the action expert are concatenated into one matrix so a single
+//     weight-streaming launch produces every modulation of a step (or of all N steps);
+//   * workspaces sized for cfg.max_batch requests, the prefix RoPE table, split-K and
+//     attention partial buffers, and the CUDA graphs of denoise_loop_kv.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <string>
+#include <tuple>
+#include <vector>
+
+#include "pi0b200.h"
+#include "attention.cuh"
+#include "common.cuh"
+#include "gemm_mma.cuh"
+#include "small_kernels.cuh"
+
+using namespace pi0;
+
+namespace {
+
+enum Role {
+  R_Q, R_K, R_V, R_O, R_GU, R_D,   // attention / MLP linears (expert e, layer l)
+  R_LN_IN, R_LN_POST,              // expert-0 plain norm weights
+  R_MOD_W, R_MOD_B,                // expert-1 modulation (block index in `layer`)
+  R_FINAL0,                        // expert-0 final norm weight (unused on the M1 path)
+  R_AIN_W, R_AIN_B, R_AOUT_W, R_AOUT_B, R_TIN_W, R_TIN_B, R_TOUT_W, R_TOUT_B
+};
+
+struct Entry {
+  std::string name;
+  int ndim;
+  int64_t shape[2];
+  int dtype;
+  Role role;
+  int expert;
+  int layer;  // layer index, or modulation block for R_MOD_*
+};
+
+struct LayerW {
+  void* qkv;   // [Hq + 2·Hkv, W]
+  void* o;     // [W, Hq]
+  void* gu;    // [2F, W] interleaved
+  void* d;     // [W, F]
+  void* ln_in;
+  void* ln_post;
+};
+
+struct GraphKey {
+  int batch;
+  const void* p[9];
+  bool operator<(const GraphKey& o) const {
+    if (batch != o.batch) return batch < o.batch;
+    return std::memcmp(p, o.p, sizeof(p)) < 0;
+  }
+};
+
+}  // namespace
+
+struct pi0_ctx {
+  pi0_config cfg{};
+  int device = 0;
+  std::string err;
+  std::vector<Entry> table;
+  bool have_params = false;
+  size_t esz = 2;
+
+  // weights
+  void* arena = nullptr;
+  size_t arena_bytes = 0;
+  std::vector<LayerW> pre, suf;
+  void *mod_w = nullptr, *mod_b = nullptr;
+  void *ain_w = nullptr, *ain_b = nullptr, *aout_w = nullptr, *aout_b = nullptr;
+  void *tin_w = nullptr, *tin_b = nullptr, *tout_w = nullptr, *tout_b = nullptr;
+  int* perm_q = nullptr;   // RoPE row permutation of a q block (H·hd rows)
+  int* perm_k = nullptr;   // ... of a k block (KV·hd rows)
+  int* perm_gu0 = nullptr; // gate/up interleave for F0
+  int* perm_gu1 = nullptr; // ... for F1
+  float* rope_cos = nullptr;  // prefix RoPE table [P, hd/2]
+  float* rope_sin = nullptr;
+
+  // workspaces
+  void *xp = nullptr, *xpn = nullptr, *attn_p = nullptr, *hp = nullptr;
+  float* qp = nullptr;
+  void *xs = nullptr, *xsn = nullptr, *attn_s = nullptr, *hs = nullptr, *vsuf = nullptr;
+  float *qs = nullptr, *ksuf = nullptr;
+  void *t1 = nullptr, *cond = nullptr, *mods = nullptr;
+  float *part_o = nullptr, *part_ml = nullptr;
+  float* splitk_ws = nullptr;
+  size_t splitk_floats = 0;
+  int* tickets = nullptr;
+  int num_sms = 148;
+
+  cudaStream_t cap_stream = nullptr;
+  std::map<GraphKey, std::pair<cudaGraphExec_t, int64_t>> graphs;  // exec, kernel nodes
+
+  // measurement
+  int64_t launches = 0;
+  bool prof_on = false;
+  struct ProfRec {
+    int fam;
+    cudaEvent_t a, b;
+  };
+  std::vector<ProfRec> prof;
+  std::vector<cudaEvent_t> ev_pool;
+
+  std::vector<void*> allocs;
+};
+
+namespace {
+
+// kernel families reported by pi0_profile_read
+enum Fam {
+  F_PRE_NORM, F_PRE_QKV, F_PRE_ATTN, F_PRE_O, F_PRE_GU, F_PRE_DOWN,
+  F_DEN_TIME_MODS, F_DEN_ACT_IN, F_DEN_NORM, F_DEN_QKV, F_DEN_ATTN, F_DEN_O, F_DEN_GU,
+  F_DEN_DOWN, F_DEN_ACT_OUT, F_NUM
+};
+const char* kFamName[F_NUM] = {
+  "prefill.rmsnorm", "prefill.qkv_rope_gemm", "prefill.attention", "prefill.o_gemm",
+  "prefill.gate_up_geglu_gemm", "prefill.down_gemm",
+  "denoise.time_mlp_modulation_gemv", "denoise.action_in", "denoise.ada_rmsnorm",
+  "denoise.qkv_rope_gemm", "denoise.attention", "denoise.o_gemm", "denoise.gate_up_geglu_gemm",
+  "denoise.down_gemm", "denoise.action_out_euler"};
+
+int fail(pi0_ctx* c, int code, const std::string& msg) {
+  if (c) c->err = msg;
+  return code;
+}
+
+#define CK(call)                                                                      \
+  do {                                                                                \
+    cudaError_t e_ = (call);                                                          \
+    if (e_ != cudaSuccess)                                                            \
+      return fail(ctx, PI0_ERR_CUDA, std::string(#call) + ": " + cudaGetErrorString(e_)); \
+  } while (0)
+
+#define CKL()                                                                         \
+  do {                                                                                \
+    cudaError_t e_ = cudaGetLastError();                                              \
+    if (e_ != cudaSuccess)                                                            \
+      return fail(ctx, PI0_ERR_CUDA, std::string("kernel launch: ") + cudaGetErrorString(e_) + \
+                                         " at " + __FILE__ + ":" + std::to_string(__LINE__)); \
+  } while (0)
+
+#define TRY(...)          \
+  do {                    \
+    int r_ = (__VA_ARGS__); \
+    if (r_) return r_;    \
+  } while (0)
+
+int dev_alloc(pi0_ctx* ctx, void** p, size_t bytes) {
+  if (bytes == 0) bytes = 16;
+  CK(cudaMalloc(p, bytes));
+  ctx->allocs.push_back(*p);
+  return 0;
+}
+
+// Brackets the launches of one kernel family with events while profiling is on.
+struct Prof {
+  pi0_ctx* c;
+  cudaStream_t st;
+  int idx = -1;
+  Prof(pi0_ctx* ctx, int fam, cudaStream_t s) : c(ctx), st(s) {
+    if (!c->prof_on) return;
+    cudaEvent_t a, b;
+    if (c->ev_pool.size() >= 2) {
+      a = c->ev_pool.back(); c->ev_pool.pop_back();
+      b = c->ev_pool.back(); c->ev_pool.pop_back();
+    } else {
+      cudaEventCreate(&a);
+      cudaEventCreate(&b);
+    }
+    cudaEventRecord(a, st);
+    c->prof.push_back({fam, a, b});
+    idx = (int)c->prof.size() - 1;
+  }
+  ~Prof() {
+    if (idx >= 0) cudaEventRecord(c->prof[idx].b, st);
+  }
+};
+
+// ---- parameter table (reference export order; see mlc_vla/model/pi0/pi0_model.py) ----------
+void build_table(pi0_ctx* c) {
+  const pi0_config& g = c->cfg;
+  const int hq = g.num_heads * g.head_dim, hkv = g.num_kv_heads * g.head_dim;
+  const int W[2] = {g.vlm_width, g.ae_width}, F[2] = {g.vlm_mlp_dim, g.ae_mlp_dim};
+  const int dt = g.dtype;
+  const bool q = g.quant != PI0_QUANT_NONE;
+  const int G = g.quant == PI0_QUANT_Q3 ? 40 : 32, epw = g.quant == PI0_QUANT_Q3 ? 10 : 8;
+  auto lin = [&](const std::string& name, int out, int in, bool bias, Role rw, Role rb, int e,
+                 int l) {
+    if (!q) {
+      c->table.push_back({name + ".weight", 2, {out, in}, dt, rw, e, l});
+    } else {
+      int64_t ng = (in + G - 1) / G;
+      c->table.push_back({name + ".q_weight", 2, {out, ng * (G / epw)}, PI0_U32, rw, e, l});
+      c->table.push_back({name + ".q_scale", 2, {out, ng}, dt, rw, e, l});
+    }
+    if (bias) c->table.push_back({name + ".bias", 1, {out, 0}, dt, rb, e, l});
+  };
+  for (int l = 0; l < g.depth; ++l) {
+    std::string p = "backbone.layers." + std::to_string(l) + ".";
+    for (int e = 0; e < 2; ++e) {
+      std::string a = p + "self_attn.experts." + std::to_string(e) + ".";
+      lin(a + "q_proj", hq, W[e], false, R_Q, R_Q, e, l);
+      lin(a + "k_proj", hkv, W[e], false, R_K, R_K, e, l);
+      lin(a + "v_proj", hkv, W[e], false, R_V, R_V, e, l);
+      lin(a + "o_proj", W[e], hq, false, R_O, R_O, e, l);
+    }
+    for (int e = 0; e < 2; ++e) {
+      std::string m = p + "mlp." + std::to_string(e) + ".";
+      lin(m + "gate_up_proj", 2 * F[e], W[e], false, R_GU, R_GU, e, l);
+      lin(m + "down_proj", W[e], F[e], false, R_D, R_D, e, l);
+    }
+    const char* lns[2] = {"input_layernorm", "post_attention_layernorm"};
+    for (int k = 0; k < 2; ++k) {
+      c->table.push_back({p + lns[k] + ".0.weight", 1, {W[0], 0}, dt, k ? R_LN_POST : R_LN_IN, 0, l});
+      lin(p + lns[k] + ".1.modulation", 3 * W[1], W[1], true, R_MOD_W, R_MOD_B, 1, 2 * l + k);
+    }
+  }
+  c->table.push_back({"backbone.final_norm.0.weight", 1, {W[0], 0}, dt, R_FINAL0, 0, 0});
+  lin("backbone.final_norm.1.modulation", 3 * W[1], W[1], true, R_MOD_W, R_MOD_B, 1, 2 * g.depth);
+  lin("action_in_proj", W[1], g.action_dim, true, R_AIN_W, R_AIN_B, 1, 0);
+  lin("action_out_proj", g.action_dim, W[1], true, R_AOUT_W, R_AOUT_B, 1, 0);
+  lin("time_mlp_in", W[1], W[1], true, R_TIN_W, R_TIN_B, 1, 0);
+  lin("time_mlp_out", W[1], W[1], true, R_TOUT_W, R_TOUT_B, 1, 0);
+}
+
+int validate(const pi0_config& g, std::string& why) {
+  auto bad = [&](const char* m) { why = m; return PI0_ERR_INVALID; };
+  if (g.dtype != PI0_F16 && g.dtype != PI0_BF16) {
+    why = "model dtype must be float16 or bfloat16 on the GPU path";
+    return PI0_ERR_UNSUPPORTED;
+  }
+  if (g.quant != PI0_QUANT_NONE && g.quant != PI0_QUANT_Q4 && g.quant != PI0_QUANT_Q3)
+    return bad("unknown quant format");
+  int hd = g.head_dim;
+  if (!(hd == 16 || hd == 32 || hd == 64 || hd == 128 || hd == 256)) {
+    why = "head_dim must be one of 16, 32, 64, 128, 256";
+    return PI0_ERR_UNSUPPORTED;
+  }
+  if (g.depth < 1 || g.num_heads < 1 || g.num_kv_heads < 1 || g.num_heads % g.num_kv_heads)
+    return bad("depth/num_heads/num_kv_heads invalid (num_heads must be a multiple of num_kv_heads)");
+  if (g.vlm_width % 32 || g.ae_width % 32 || g.vlm_mlp_dim % 32 || g.ae_mlp_dim % 32 ||
+      (g.num_heads * hd) % 32)
+    return bad("widths, mlp dims and num_heads*head_dim must be multiples of 32");
+  if (g.vlm_width <= 0 || g.ae_width <= 0 || g.vlm_mlp_dim <= 0 || g.ae_mlp_dim <= 0)
+    return bad("widths and mlp dims must be positive");
+  if (g.prefix_len < 1 || g.action_horizon < 1 || g.action_dim < 1 || g.num_denoise_steps < 1)
+    return bad("prefix_len, action_horizon, action_dim and num_denoise_steps must be >= 1");
+  if (g.max_batch < 1) return bad("max_batch must be >= 1");
+  if (g.ae_width > 4096) return bad("action-expert width above 4096 is not supported");
+  return 0;
+}
+
+
+// ---- GEMM launch --------------------------------------------------------------------------
+template <typename T, int BM, int BN, int WM, int WN, int ST, class Epi>
+int gemm_launch_cfg(pi0_ctx* ctx, const T* A, int lda, const T* W, int ldw, int M, int N, int K,
+                    const Epi& epi, int splits, cudaStream_t st, int fam) {
+  using C = GemmCfg<T, BM, BN, WM, WN, ST>;
+  auto kern = gemm_mma_kernel<T, BM, BN, WM, WN, ST, Epi>;
+  GemmArgs<T> g{A, lda, W, ldw, M, N, K, 0, ctx->splitk_ws, ctx->tickets};
+  int ksteps = K / 32;
+  splits = std::max(1, std::min(splits, ksteps));
+  int per = (ksteps + splits - 1) / splits;
+  splits = (ksteps + per - 1) / per;
+  g.k_split_len = per * 32;
+  dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM, splits);
+  if (splits > 1) {
+    if ((size_t)splits * M * N > ctx->splitk_floats)
+      return fail(ctx, PI0_ERR_INVALID, "split-K workspace too small");
+    if ((size_t)grid.x * grid.y > (1u << 16)) return fail(ctx, PI0_ERR_INVALID, "too many tiles");
+  }
+  Prof pr(ctx, fam, st);
+  kern<<<grid, C::NT, C::SMEM, st>>>(g, epi);
+  ctx->launches += 1;
+  CKL();
+  return 0;
+}
+
+template <typename T, class Epi>
+int gemm(pi0_ctx* ctx, const T* A, int lda, const T* W, int ldw, int M, int N, int K,
+         const Epi& epi, cudaStream_t st, int fam) {
+  if (M >= 256) {
+    return gemm_launch_cfg<T, 128, 128, 64, 32, 4>(ctx, A, lda, W, ldw, M, N, K, epi, 1, st, fam);
+  }
+  int tiles = ((M + 63) / 64) * ((N + 63) / 64);
+  int splits = std::max(1, (2 * ctx->num_sms + tiles - 1) / tiles);
+  splits = std::min(splits, std::max(1, K / 128));
+  return gemm_launch_cfg<T, 64, 64, 32, 32, 4>(ctx, A, lda, W, ldw, M, N, K, epi, splits, st, fam);
+}
+
+// ---- attention launch ----------------------------------------------------------------------
+// Key splits: enough CTAs for two waves over the SMs; keys_per_split is a multiple of ATT_BK.
+int attn_kps(int rows, int batch, int KV, int ltot, int num_sms, bool allow_split) {
+  const int row_tiles = (rows + ATT_BQ - 1) / ATT_BQ;
+  int splits = 1;
+  if (allow_split) {
+    int ctas = row_tiles * batch * KV;
+    splits = std::max(1, (2 * num_sms + ctas - 1) / ctas);
+    splits = std::min(splits, (ltot + ATT_BK - 1) / ATT_BK);
+  }
+  int kps = (ltot + splits - 1) / splits;
+  return (kps + ATT_BK - 1) / ATT_BK * ATT_BK;
+}
+int attn_splits(int rows, int batch, int KV, int ltot, int num_sms, bool allow_split) {
+  int kps = attn_kps(rows, batch, KV, ltot, num_sms, allow_split);
+  return (ltot + kps - 1) / kps;
+}
+
+template <typename T, int HD>
+int attn_launch_hd(pi0_ctx* ctx, AttnArgs<T> a, int batch, bool allow_split, cudaStream_t st,
+                   int fam) {
+  Prof pr(ctx, fam, st);
+  const int G = a.H / a.KV, rows = a.Tq * G;
+  const int row_tiles = (rows + ATT_BQ - 1) / ATT_BQ;
+  const int ltot = a.LA + a.LB;
+  const int kps = attn_kps(rows, batch, a.KV, ltot, ctx->num_sms, allow_split);
+  const int splits = (ltot + kps - 1) / kps;
+  a.keys_per_split = kps;
+  auto kern = attn_kernel<T, HD>;
+  dim3 grid(row_tiles, splits, batch * a.KV);
+  kern<<<grid, 128, AttnSmem<HD>::BYTES, st>>>(a);
+  ctx->launches += 1;
+  CKL();
+  if (splits > 1) {
+    dim3 g2(rows, batch * a.KV);
+    attn_combine_kernel<T><<<g2, std::max(32, std::min(128, HD / 2)), 0, st>>>(a, HD, splits);
+    ctx->launches += 1;
+    CKL();
+  }
+  return 0;
+}
+
+template <typename T>
+int attn_launch(pi0_ctx* ctx, AttnArgs<T> a, int batch, bool allow_split, cudaStream_t st,
+                int fam) {
+  switch (ctx->cfg.head_dim) {
+    case 16: return attn_launch_hd<T, 16>(ctx, a, batch, allow_split, st, fam);
+    case 32: return attn_launch_hd<T, 32>(ctx, a, batch, allow_split, st, fam);
+    case 64: return attn_launch_hd<T, 64>(ctx, a, batch, allow_split, st, fam);
+    case 128: return attn_launch_hd<T, 128>(ctx, a, batch, allow_split, st, fam);
+    case 256: return attn_launch_hd<T, 256>(ctx, a, batch, allow_split, st, fam);
+  }
+  return fail(ctx, PI0_ERR_UNSUPPORTED, "head_dim");
+}
+
+
+template <typename T>
+int rmsnorm(pi0_ctx* ctx, const T* x, T* out, int rows, int W, const T* w, const T* mod,
+            int rows_per_mod, int mod_stride, cudaStream_t st, int fam) {
+  Prof pr(ctx, fam, st);
+  ctx->launches += 1;
+  int blocks = (rows + 7) / 8;
+  rmsnorm_kernel<T><<<blocks, 256, 0, st>>>(x, out, rows, W, ctx->cfg.rms_norm_eps, w, mod,
+                                            rows_per_mod, mod_stride);
+  CKL();
+  return 0;
+}
+
+template <typename T>
+int gemv(pi0_ctx* ctx, const T* x, int M, int K, const T* W, const T* b, int N, T* y, int ldy,
+         int silu, cudaStream_t st) {
+  Prof pr(ctx, F_DEN_TIME_MODS, st);
+  for (int m0 = 0; m0 < M; m0 += GEMV_MMAX) {
+    ctx->launches += 1;
+    int mm = std::min(GEMV_MMAX, M - m0);
+    size_t smem = (size_t)mm * K * sizeof(float);
+    int blocks = std::min((N + 7) / 8, ctx->num_sms * 8);
+    gemv_kernel<T><<<blocks, 256, smem, st>>>(x + (size_t)m0 * K, mm, K, W, b, N,
+                                              y + (size_t)m0 * ldy, ldy, silu);
+    CKL();
+  }
+  return 0;
+}
+
+// time conditions and all 2·L+1 modulations for `nsteps` time embeddings [nsteps, W1]
+template <typename T>
+int time_and_mods(pi0_ctx* ctx, const T* te, int nsteps, cudaStream_t st) {
+  const pi0_config& g = ctx->cfg;
+  const int W1 = g.ae_width;
+  const int nmod = (2 * g.depth + 1) * 3 * W1;
+  T* t1 = (T*)ctx->t1;
+  T* cond = (T*)ctx->cond;
+  TRY(gemv<T>(ctx, te, nsteps, W1, (const T*)ctx->tin_w, (const T*)ctx->tin_b, W1, t1, W1, 1, st));
+  TRY(gemv<T>(ctx, t1, nsteps, W1, (const T*)ctx->tout_w, (const T*)ctx->tout_b, W1, cond, W1, 1, st));
+  TRY(gemv<T>(ctx, cond, nsteps, W1, (const T*)ctx->mod_w, (const T*)ctx->mod_b, nmod,
+              (T*)ctx->mods, nmod, 0, st));
+  return 0;
+}
+
+// ---- prefill ---------------------------------------------------------------------------------
+template <typename T>
+int run_prefill(pi0_ctx* ctx, int B, const T* prefix, const float* mask, float* keys, T* values,
+                cudaStream_t st) {
+  const pi0_config& g = ctx->cfg;
+  const int P = g.prefix_len, W0 = g.vlm_width, F0 = g.vlm_mlp_dim, hd = g.head_dim;
+  const int H = g.num_heads, KV = g.num_kv_heads, hq = H * hd, hkv = KV * hd;
+  const int M = B * P;
+  T* x = (T*)ctx->xp;
+  T* xn = (T*)ctx->xpn;
+  T* attn = (T*)ctx->attn_p;
+  T* h = (T*)ctx->hp;
+  CK(cudaMemcpyAsync(x, prefix, (size_t)M * W0 * sizeof(T), cudaMemcpyDeviceToDevice, st));
+  const size_t kv_layer = (size_t)B * KV * P * hd;
+  for (int l = 0; l < g.depth; ++l) {
+    const LayerW& w = ctx->pre[l];
+    float* kl = keys + l * kv_layer;
+    T* vl = values + l * kv_layer;
+    TRY(rmsnorm<T>(ctx, x, xn, M, W0, (const T*)w.ln_in, nullptr, 1, 0, st, F_PRE_NORM));
+    EpiQkvRope<T> eq{ctx->qp, kl, vl, ctx->rope_cos, ctx->rope_sin, 0, P, H, KV, hd, 0,
+                     (float)std::pow((double)hd, -0.5)};
+    const bool last = l == g.depth - 1;
+    if (last) {  // only k and v of the last layer are ever read
+      eq.col0 = hq;
+      TRY(gemm<T>(ctx, xn, W0, (const T*)w.qkv + (size_t)hq * W0, W0, M, 2 * hkv, W0, eq, st,
+                  F_PRE_QKV));
+      break;
+    }
+    TRY(gemm<T>(ctx, xn, W0, (const T*)w.qkv, W0, M, hq + 2 * hkv, W0, eq, st, F_PRE_QKV));
+    AttnArgs<T> a{};
+    a.q = ctx->qp;
+    a.kA = kl;
+    a.vA = vl;
+    a.maskA = mask;
+    a.LA = P;
+    a.kB = nullptr;
+    a.vB = nullptr;
+    a.LB = 0;
+    a.Tq = P;
+    a.H = H;
+    a.KV = KV;
+    a.out = attn;
+    a.part_o = ctx->part_o;
+    a.part_ml = ctx->part_ml;
+    TRY(attn_launch<T>(ctx, a, B, false, st, F_PRE_ATTN));
+    TRY(gemm<T>(ctx, attn, hq, (const T*)w.o, hq, M, W0, hq, EpiResid<T>{x, W0}, st, F_PRE_O));
+    TRY(rmsnorm<T>(ctx, x, xn, M, W0, (const T*)w.ln_post, nullptr, 1, 0, st, F_PRE_NORM));
+    TRY(gemm<T>(ctx, xn, W0, (const T*)w.gu, W0, M, 2 * F0, W0, EpiGeglu<T>{h, F0}, st,
+                F_PRE_GU));
+    TRY(gemm<T>(ctx, h, F0, (const T*)w.d, F0, M, W0, F0, EpiResid<T>{x, W0}, st, F_PRE_DOWN));
+  }
+  return 0;
+}
+
+// ---- one suffix pass (decode_suffix + action_out) with modulations `mods` -------------------
+// x_in: model-dtype x_t (x_is_f32 = false) or the fp32 Euler state (x_is_f32 = true).
+// out: v (euler = 0) or the fp32 state updated in place by x += dt·v (euler = 1).
+template <typename T>
+int run_suffix(pi0_ctx* ctx, int B, const float* keys, const T* values, const void* x_in,
+               bool x_is_f32, const T* mods, const float* scos, const float* ssin,
+               const float* mask, float* out, int euler, float dt, cudaStream_t st) {
+  const pi0_config& g = ctx->cfg;
+  const int P = g.prefix_len, S = g.action_horizon, D = g.action_dim, W1 = g.ae_width;
+  const int F1 = g.ae_mlp_dim, hd = g.head_dim, H = g.num_heads, KV = g.num_kv_heads;
+  const int hq = H * hd, hkv = KV * hd, M = B * S;
+  const int mstride = 3 * W1;
+  T* x = (T*)ctx->xs;
+  T* xn = (T*)ctx->xsn;
+  T* attn = (T*)ctx->attn_s;
+  T* h = (T*)ctx->hs;
+  {
+    Prof pr(ctx, F_DEN_ACT_IN, st);
+    ctx->launches += 1;
+    int n = M * W1;
+    if (x_is_f32)
+      action_in_kernel<T, true><<<(n + 255) / 256, 256, 0, st>>>(x_in, M, D, (const T*)ctx->ain_w,
+                                                                 (const T*)ctx->ain_b, W1, x);
+    else
+      action_in_kernel<T, false><<<(n + 255) / 256, 256, 0, st>>>(x_in, M, D, (const T*)ctx->ain_w,
+                                                                  (const T*)ctx->ain_b, W1, x);
+    CKL();
+  }
+  const size_t kv_layer = (size_t)B * KV * P * hd;
+  for (int l = 0; l < g.depth; ++l) {
+    const LayerW& w = ctx->suf[l];
+    const T* m_in = mods + (size_t)(2 * l) * mstride;
+    const T* m_post = mods + (size_t)(2 * l + 1) * mstride;
+    TRY(rmsnorm<T>(ctx, x, xn, M, W1, nullptr, m_in, M, 0, st, F_DEN_NORM));
+    EpiQkvRope<T> eq{ctx->qs, ctx->ksuf, (T*)ctx->vsuf, scos, ssin, S * (hd / 2), S, H, KV, hd, 0,
+                     (float)std::pow((double)hd, -0.5)};
+    TRY(gemm<T>(ctx, xn, W1, (const T*)w.qkv, W1, M, hq + 2 * hkv, W1, eq, st, F_DEN_QKV));
+    AttnArgs<T> a{};
+    a.q = ctx->qs;
+    a.kA = keys + l * kv_layer;
+    a.vA = values + l * kv_layer;
+    a.maskA = mask;
+    a.LA = P;
+    a.kB = ctx->ksuf;
+    a.vB = (const T*)ctx->vsuf;
+    a.LB = S;
+    a.Tq = S;
+    a.H = H;
+    a.KV = KV;
+    a.out = attn;
+    a.part_o = ctx->part_o;
+    a.part_ml = ctx->part_ml;
+    TRY(attn_launch<T>(ctx, a, B, true, st, F_DEN_ATTN));
+    TRY(gemm<T>(ctx, attn, hq, (const T*)w.o, hq, M, W1, hq,
+                EpiGatedResid<T>{x, W1, m_in + 2 * W1, M, 0}, st, F_DEN_O));
+    TRY(rmsnorm<T>(ctx, x, xn, M, W1, nullptr, m_post, M, 0, st, F_DEN_NORM));
+    TRY(gemm<T>(ctx, xn, W1, (const T*)w.gu, W1, M, 2 * F1, W1, EpiGeglu<T>{h, F1}, st,
+                F_DEN_GU));
+    TRY(gemm<T>(ctx, h, F1, (const T*)w.d, F1, M, W1, F1,
+                EpiGatedResid<T>{x, W1, m_post + 2 * W1, M, 0}, st, F_DEN_DOWN));
+  }
+  TRY(rmsnorm<T>(ctx, x, xn, M, W1, nullptr, mods + (size_t)(2 * g.depth) * mstride, M, 0, st,
+                 F_DEN_NORM));
+  {
+    Prof pr(ctx, F_DEN_ACT_OUT, st);
+    ctx->launches += 1;
+    int warps = M * D;
+    action_out_kernel<T><<<(warps * 32 + 255) / 256, 256, 0, st>>>(
+        xn, M, W1, (const T*)ctx->aout_w, (const T*)ctx->aout_b, D, out, euler, dt);
+    CKL();
+  }
+  return 0;
+}
+
+template <typename T>
+int run_step(pi0_ctx* ctx, int B, const float* keys, const T* values, const T* x_t, const T* te,
+             const float* scos, const float* ssin, const float* mask, float* v_out,
+             cudaStream_t st) {
+  TRY(time_and_mods<T>(ctx, te, 1, st));
+  return run_suffix<T>(ctx, B, keys, values, x_t, false, (const T*)ctx->mods, scos, ssin, mask,
+                       v_out, 0, 0.f, st);
+}
+
+template <typename T>
+int run_loop_body(pi0_ctx* ctx, int B, const float* keys, const T* values, const float* x0,
+                  const T* tes, const float* scos, const float* ssin, const float* mask,
+                  float* x_out, cudaStream_t st) {
+  const pi0_config& g = ctx->cfg;
+  const int N = g.num_denoise_steps;
+  const size_t nmod = (size_t)(2 * g.depth + 1) * 3 * g.ae_width;
+  if (x_out != x0)
+    CK(cudaMemcpyAsync(x_out, x0, (size_t)B * g.action_horizon * g.action_dim * sizeof(float),
+                       cudaMemcpyDeviceToDevice, st));
+  TRY(time_and_mods<T>(ctx, tes, N, st));
+  const float dt = (float)(-1.0 / N);
+  for (int i = 0; i < N; ++i)
+    TRY(run_suffix<T>(ctx, B, keys, values, x_out, true, (const T*)ctx->mods + i * nmod, scos,
+                      ssin, mask, x_out, 1, dt, st));
+  return 0;
+}
+
+// ---- kernel attributes (set once at context creation: never inside a graph capture) --------
+template <typename T, int BM, int BN, int WM, int WN, int ST, class Epi>
+int attr_gemm(pi0_ctx* ctx) {
+  CK(cudaFuncSetAttribute(gemm_mma_kernel<T, BM, BN, WM, WN, ST, Epi>,
+                          cudaFuncAttributeMaxDynamicSharedMemorySize,
+                          GemmCfg<T, BM, BN, WM, WN, ST>::SMEM));
+  return 0;
+}
+template <typename T, class Epi>
+int attr_gemm_both(pi0_ctx* ctx) {
+  TRY((attr_gemm<T, 128, 128, 64, 32, 4, Epi>(ctx)));
+  TRY((attr_gemm<T, 64, 64, 32, 32, 4, Epi>(ctx)));
+  return 0;
+}
+template <typename T, int HD>
+int attr_attn(pi0_ctx* ctx) {
+  CK(cudaFuncSetAttribute(attn_kernel<T, HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                          AttnSmem<HD>::BYTES));
+  return 0;
+}
+template <typename T>
+int setup_attrs(pi0_ctx* ctx) {
+  TRY(attr_gemm_both<T, EpiQkvRope<T>>(ctx));
+  TRY(attr_gemm_both<T, EpiResid<T>>(ctx));
+  TRY(attr_gemm_both<T, EpiGatedResid<T>>(ctx));
+  TRY(attr_gemm_both<T, EpiGeglu<T>>(ctx));
+  switch (ctx->cfg.head_dim) {
+    case 16: TRY((attr_attn<T, 16>(ctx))); break;
+    case 32: TRY((attr_attn<T, 32>(ctx))); break;
+    case 64: TRY((attr_attn<T, 64>(ctx))); break;
+    case 128: TRY((attr_attn<T, 128>(ctx))); break;
+    case 256: TRY((attr_attn<T, 256>(ctx))); break;
+  }
+  int gemv_smem = GEMV_MMAX * std::max(ctx->cfg.ae_width, 1) * 4;
+  CK(cudaFuncSetAttribute(gemv_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, gemv_smem));
+  return 0;
+}
+
+// ---- set params ---------------------------------------------------------------------------
+int upload_ints(pi0_ctx* ctx, int** dst, const std::vector<int>& v) {
+  TRY(dev_alloc(ctx, (void**)dst, v.size() * sizeof(int)));
+  CK(cudaMemcpy(*dst, v.data(), v.size() * sizeof(int), cudaMemcpyHostToDevice));
+  return 0;
+}
+
+std::vector<int> rope_perm(int heads, int hd) {
+  // packed row h·hd + 2i + c  <-  original row h·hd + i + c·hd/2
+  std::vector<int> p(heads * hd);
+  for (int h = 0; h < heads; ++h)
+    for (int i = 0; i < hd / 2; ++i)
+      for (int c = 0; c < 2; ++c) p[h * hd + 2 * i + c] = h * hd + i + c * (hd / 2);
+  return p;
+}
+std::vector<int> gu_perm(int F) {
+  // packed row 2j = gate row j, 2j + 1 = up row j (= original row F + j)
+  std::vector<int> p(2 * F);
+  for (int j = 0; j < F; ++j) {
+    p[2 * j] = j;
+    p[2 * j + 1] = F + j;
+  }
+  return p;
+}
+
+int gather(pi0_ctx* ctx, void* dst, const void* src, const int* idx, int rows, int K,
+           cudaStream_t st) {
+  gather_rows_kernel<<<rows, 128, 0, st>>>((uint16_t*)dst, (const uint16_t*)src, idx, rows, K);
+  CKL();
+  return 0;
+}
+
+int copy(pi0_ctx* ctx, void* dst, const void* src, size_t bytes, cudaStream_t st) {
+  CK(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, st));
+  return 0;
+}
+
+int alloc_all(pi0_ctx* ctx) {
+  const pi0_config& g = ctx->cfg;
+  const size_t e = ctx->esz;
+  const int L = g.depth, hd = g.head_dim, H = g.num_heads, KV = g.num_kv_heads;
+  const size_t hq = (size_t)H * hd, hkv = (size_t)KV * hd;
+  const size_t W0 = g.vlm_width, W1 = g.ae_width, F0 = g.vlm_mlp_dim, F1 = g.ae_mlp_dim;
+  const size_t B = g.max_batch, P = g.prefix_len, S = g.action_horizon, D = g.action_dim;
+  const int N = g.num_denoise_steps;
+
+  // weight arena: every block starts on a 256-byte boundary
+  const size_t nmodw = (size_t)(2 * L + 1) * 3 * W1;
+  auto pad = [&](size_t elems) { return ((elems * e + 255) / 256) * 256; };
+  size_t arena = 0;
+  for (int l = 0; l < L; ++l)
+    arena += pad((hq + 2 * hkv) * W0) + pad(W0 * hq) + pad(2 * F0 * W0) + pad(W0 * F0) +
+             2 * pad(W0) + pad((hq + 2 * hkv) * W1) + pad(W1 * hq) + pad(2 * F1 * W1) +
+             pad(W1 * F1);
+  arena += pad(nmodw * W1) + pad(nmodw) + pad(W1 * D) + pad(W1) + pad(D * W1) + pad(D) +
+           2 * (pad(W1 * W1) + pad(W1));
+  ctx->arena_bytes = arena;
+  TRY(dev_alloc(ctx, &ctx->arena, ctx->arena_bytes));
+  char* p = (char*)ctx->arena;
+  auto take = [&](size_t elems) {
+    void* r = p;
+    p += pad(elems);
+    return r;
+  };
+  ctx->pre.resize(L);
+  ctx->suf.resize(L);
+  for (int l = 0; l < L; ++l) {
+    LayerW& a = ctx->pre[l];
+    a.qkv = take((hq + 2 * hkv) * W0);
+    a.o = take(W0 * hq);
+    a.gu = take(2 * F0 * W0);
+    a.d = take(W0 * F0);
+    a.ln_in = take(W0);
+    a.ln_post = take(W0);
+    LayerW& s = ctx->suf[l];
+    s.qkv = take((hq + 2 * hkv) * W1);
+    s.o = take(W1 * hq);
+    s.gu = take(2 * F1 * W1);
+    s.d = take(W1 * F1);
+    s.ln_in = s.ln_post = nullptr;
+  }
+  ctx->mod_w = take(nmodw * W1);
+  ctx->mod_b = take(nmodw);
+  ctx->ain_w = take(W1 * D);
+  ctx->ain_b = take(W1);
+  ctx->aout_w = take(D * W1);
+  ctx->aout_b = take(D);
+  ctx->tin_w = take(W1 * W1);
+  ctx->tin_b = take(W1);
+  ctx->tout_w = take(W1 * W1);
+  ctx->tout_b = take(W1);
+
+  // permutations and the prefix RoPE table (float64 -> fp32, gemma_dual.py:24-44)
+  TRY(upload_ints(ctx, &ctx->perm_q, rope_perm(H, hd)));
+  TRY(upload_ints(ctx, &ctx->perm_k, rope_perm(KV, hd)));
+  TRY(upload_ints(ctx, &ctx->perm_gu0, gu_perm((int)F0)));
+  TRY(upload_ints(ctx, &ctx->perm_gu1, gu_perm((int)F1)));
+  {
+    std::vector<float> c(P * (hd / 2)), s(P * (hd / 2));
+    for (size_t t = 0; t < P; ++t)
+      for (int i = 0; i < hd / 2; ++i) {
+        double ts = std::pow((double)g.rope_theta, (2.0 / hd) * i);
+        double r = (double)t / ts;
+        c[t * (hd / 2) + i] = (float)std::cos(r);
+        s[t * (hd / 2) + i] = (float)std::sin(r);
+      }
+    TRY(dev_alloc(ctx, (void**)&ctx->rope_cos, c.size() * 4));
+    TRY(dev_alloc(ctx, (void**)&ctx->rope_sin, s.size() * 4));
+    CK(cudaMemcpy(ctx->rope_cos, c.data(), c.size() * 4, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(ctx->rope_sin, s.data(), s.size() * 4, cudaMemcpyHostToDevice));
+  }
+
+  // workspaces
+  const size_t MP = B * P, MS = B * S;
+  TRY(dev_alloc(ctx, &ctx->xp, MP * W0 * e));
+  TRY(dev_alloc(ctx, &ctx->xpn, MP * W0 * e));
+  TRY(dev_alloc(ctx, &ctx->attn_p, MP * hq * e));
+  TRY(dev_alloc(ctx, &ctx->hp, MP * F0 * e));
+  TRY(dev_alloc(ctx, (void**)&ctx->qp, MP * hq * 4));
+  TRY(dev_alloc(ctx, &ctx->xs, MS * W1 * e));
+  TRY(dev_alloc(ctx, &ctx->xsn, MS * W1 * e));
+  TRY(dev_alloc(ctx, &ctx->attn_s, MS * hq * e));
+  TRY(dev_alloc(ctx, &ctx->hs, MS * F1 * e));
+  TRY(dev_alloc(ctx, (void**)&ctx->qs, MS * hq * 4));
+  TRY(dev_alloc(ctx, (void**)&ctx->ksuf, B * hkv * S * 4));
+  TRY(dev_alloc(ctx, &ctx->vsuf, B * hkv * S * e));
+  TRY(dev_alloc(ctx, &ctx->t1, (size_t)N * W1 * e));
+  TRY(dev_alloc(ctx, &ctx->cond, (size_t)N * W1 * e));
+  TRY(dev_alloc(ctx, &ctx->mods, (size_t)N * nmodw * e));
+  // attention split partials of the denoise attention: max over batch sizes of B·splits(B)
+  const int rows = (int)S * (H / KV);
+  size_t bs_max = 1;
+  for (int b = 1; b <= (int)B; ++b)
+    bs_max = std::max(bs_max, (size_t)b * attn_splits(rows, b, KV, (int)(P + S), ctx->num_sms, true));
+  TRY(dev_alloc(ctx, (void**)&ctx->part_o, bs_max * KV * rows * hd * 4));
+  TRY(dev_alloc(ctx, (void**)&ctx->part_ml, bs_max * KV * rows * 2 * 4));
+  // split-K partials (GEMMs with M < 256 only): splits·M·N ≤ (2·SMs/tiles + 1)·M·N
+  //   ≤ 2·SMs·64·64 + 256·maxN
+  size_t maxN = std::max(std::max(hq + 2 * hkv, 2 * F1), std::max(std::max(W1, W0), 2 * F0));
+  ctx->splitk_floats = (size_t)2 * ctx->num_sms * 64 * 64 + 256 * maxN;
+  TRY(dev_alloc(ctx, (void**)&ctx->splitk_ws, ctx->splitk_floats * 4));
+  TRY(dev_alloc(ctx, (void**)&ctx->tickets, (1 << 16) * 4));
+  CK(cudaMemset(ctx->tickets, 0, (1 << 16) * 4));
+  return 0;
+}
+
+template <typename T>
+int set_params_impl(pi0_ctx* ctx, const void* const* params, cudaStream_t st) {
+  const pi0_config& g = ctx->cfg;
+  const int hd = g.head_dim, H = g.num_heads, KV = g.num_kv_heads;
+  const size_t hq = (size_t)H * hd, hkv = (size_t)KV * hd;
+  const size_t W[2] = {(size_t)g.vlm_width, (size_t)g.ae_width};
+  const size_t F[2] = {(size_t)g.vlm_mlp_dim, (size_t)g.ae_mlp_dim};
+  const size_t e = sizeof(T);
+  const size_t W1 = g.ae_width;
+  for (size_t i = 0; i < ctx->table.size(); ++i) {
+    const Entry& en = ctx->table[i];
+    const void* src = params[i];
+    if (!src) return fail(ctx, PI0_ERR_INVALID, "null pointer for parameter " + en.name);
+    const int l = en.layer, ex = en.expert;
+    LayerW* lw = nullptr;
+    if (en.role <= R_D) lw = ex == 0 ? &ctx->pre[l] : &ctx->suf[l];
+    const size_t Wd = W[ex];
+    switch (en.role) {
+      case R_Q: TRY(gather(ctx, lw->qkv, src, ctx->perm_q, (int)hq, (int)Wd, st)); break;
+      case R_K:
+        TRY(gather(ctx, (char*)lw->qkv + hq * Wd * e, src, ctx->perm_k, (int)hkv, (int)Wd, st));
+        break;
+      case R_V: TRY(copy(ctx, (char*)lw->qkv + (hq + hkv) * Wd * e, src, hkv * Wd * e, st)); break;
+      case R_O: TRY(copy(ctx, lw->o, src, Wd * hq * e, st)); break;
+      case R_GU:
+        TRY(gather(ctx, lw->gu, src, ex == 0 ? ctx->perm_gu0 : ctx->perm_gu1, (int)(2 * F[ex]),
+                   (int)Wd, st));
+        break;
+      case R_D: TRY(copy(ctx, lw->d, src, Wd * F[ex] * e, st)); break;
+      case R_LN_IN: TRY(copy(ctx, ctx->pre[l].ln_in, src, W[0] * e, st)); break;
+      case R_LN_POST: TRY(copy(ctx, ctx->pre[l].ln_post, src, W[0] * e, st)); break;
+      case R_MOD_W:
+        TRY(copy(ctx, (char*)ctx->mod_w + (size_t)l * 3 * W1 * W1 * e, src, 3 * W1 * W1 * e, st));
+        break;
+      case R_MOD_B:
+        TRY(copy(ctx, (char*)ctx->mod_b + (size_t)l * 3 * W1 * e, src, 3 * W1 * e, st));
+        break;
+      case R_FINAL0: break;  // the prefix expert's final norm feeds nothing on the M1 path
+      case R_AIN_W: TRY(copy(ctx, ctx->ain_w, src, W1 * g.action_dim * e, st)); break;
+      case R_AIN_B: TRY(copy(ctx, ctx->ain_b, src, W1 * e, st)); break;
+      case R_AOUT_W: TRY(copy(ctx, ctx->aout_w, src, W1 * g.action_dim * e, st)); break;
+      case R_AOUT_B: TRY(copy(ctx, ctx->aout_b, src, g.action_dim * e, st)); break;
+      case R_TIN_W: TRY(copy(ctx, ctx->tin_w, src, W1 * W1 * e, st)); break;
+      case R_TIN_B: TRY(copy(ctx, ctx->tin_b, src, W1 * e, st)); break;
+      case R_TOUT_W: TRY(copy(ctx, ctx->tout_w, src, W1 * W1 * e, st)); break;
+      case R_TOUT_B: TRY(copy(ctx, ctx->tout_b, src, W1 * e, st)); break;
+    }
+  }
+  return 0;
+}
+
+bool is_bf16(const pi0_ctx* c) { return c->cfg.dtype == PI0_BF16; }
+
+int check_ready(pi0_ctx* ctx, int batch) {
+  if (!ctx) return PI0_ERR_INVALID;
+  if (!ctx->have_params) return fail(ctx, PI0_ERR_NO_PARAMS, "pi0_set_params has not been called");
+  if (batch < 1 || batch > ctx->cfg.max_batch)
+    return fail(ctx, PI0_ERR_INVALID, "batch must be in [1, max_batch]");
+  cudaError_t e = cudaSetDevice(ctx->device);
+  if (e != cudaSuccess) return fail(ctx, PI0_ERR_CUDA, cudaGetErrorString(e));
+  return 0;
+}
+
+}  // namespace
+
+// =============================================================================================
+// C ABI
+// =============================================================================================
+extern "C" {
+
+int pi0_create(const pi0_config* cfg, int device, pi0_ctx** out) {
+  if (!cfg || !out) return PI0_ERR_INVALID;
+  *out = nullptr;
+  pi0_ctx* ctx = new pi0_ctx();
+  ctx->cfg = *cfg;
+  ctx->device = device;
+  std::string why;
+  int r = validate(*cfg, why);
+  if (r) {
+    *out = ctx;
+    return fail(ctx, r, why);
+  }
+  ctx->esz = 2;
+  build_table(ctx);
+  *out = ctx;
+  if (cfg->quant != PI0_QUANT_NONE)
+    return fail(ctx, PI0_ERR_UNSUPPORTED, "quantised weights are not implemented in this build yet");
+  CK(cudaSetDevice(device));
+  int sms = 0;
+  CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
+  ctx->num_sms = sms;
+  CK(cudaStreamCreateWithFlags(&ctx->cap_stream, cudaStreamNonBlocking));
+  TRY(alloc_all(ctx));
+  TRY(is_bf16(ctx) ? setup_attrs<__nv_bfloat16>(ctx) : setup_attrs<__half>(ctx));
+  return 0;
+}
+
+int pi0_destroy(pi0_ctx* ctx) {
+  if (!ctx) return 0;
+  cudaSetDevice(ctx->device);
+  for (auto& kv : ctx->graphs) cudaGraphExecDestroy(kv.second.first);
+  for (auto& r : ctx->prof) {
+    cudaEventDestroy(r.a);
+    cudaEventDestroy(r.b);
+  }
+  for (auto e : ctx->ev_pool) cudaEventDestroy(e);
+  if (ctx->cap_stream) cudaStreamDestroy(ctx->cap_stream);
+  for (void* p : ctx->allocs) cudaFree(p);
+  delete ctx;
+  return 0;
+}
+
+const char* pi0_last_error(const pi0_ctx* ctx) { return ctx ? ctx->err.c_str() : "null context"; }
+
+int pi0_num_params(const pi0_ctx* ctx) { return ctx ? (int)ctx->table.size() : -1; }
+
+int pi0_param_info(const pi0_ctx* ctx, int i, const char** name, int* ndim, int64_t shape[2],
+                   int* dtype) {
+  if (!ctx || i < 0 || i >= (int)ctx->table.size()) return PI0_ERR_INVALID;
+  const Entry& e = ctx->table[i];
+  if (name) *name = e.name.c_str();
+  if (ndim) *ndim = e.ndim;
+  if (shape) {
+    shape[0] = e.shape[0];
+    shape[1] = e.shape[1];
+  }
+  if (dtype) *dtype = e.dtype;
+  return 0;
+}
+
+int pi0_set_params(pi0_ctx* ctx, const void* const* params, int n, pi0_stream_t stream) {
+  if (!ctx || !params) return PI0_ERR_INVALID;
+  if (n != (int)ctx->table.size())
+    return fail(ctx, PI0_ERR_INVALID, "expected " + std::to_string(ctx->table.size()) +
+                                          " parameters, got " + std::to_string(n));
+  CK(cudaSetDevice(ctx->device));
+  int r = is_bf16(ctx) ? set_params_impl<__nv_bfloat16>(ctx, params, stream)
+                       : set_params_impl<__half>(ctx, params, stream);
+  if (r) return r;
+  ctx->have_params = true;
+  for (auto& kv : ctx->graphs) cudaGraphExecDestroy(kv.second.first);
+  ctx->graphs.clear();
+  return 0;
+}
+
+int pi0_prefill(pi0_ctx* ctx, int batch, const void* prefix_embs, const float* prefix_mask,
+                float* keys, void* values, pi0_stream_t stream) {
+  TRY(check_ready(ctx, batch));
+  if (!prefix_embs || !prefix_mask || !keys || !values)
+    return fail(ctx, PI0_ERR_INVALID, "null tensor argument");
+  if (is_bf16(ctx))
+    return run_prefill<__nv_bfloat16>(ctx, batch, (const __nv_bfloat16*)prefix_embs, prefix_mask,
+                                      keys, (__nv_bfloat16*)values, stream);
+  return run_prefill<__half>(ctx, batch, (const __half*)prefix_embs, prefix_mask, keys,
+                             (__half*)values, stream);
+}
+
+int pi0_denoise_step_kv(pi0_ctx* ctx, int batch, const float* keys, const void* values,
+                        const void* x_t, const void* time_emb, const float* suffix_cos,
+                        const float* suffix_sin, const float* prefix_mask, float* v_out,
+                        pi0_stream_t stream) {
+  TRY(check_ready(ctx, batch));
+  if (!keys || !values || !x_t || !time_emb || !suffix_cos || !suffix_sin || !prefix_mask || !v_out)
+    return fail(ctx, PI0_ERR_INVALID, "null tensor argument");
+  if (is_bf16(ctx))
+    return run_step<__nv_bfloat16>(ctx, batch, keys, (const __nv_bfloat16*)values,
+                                   (const __nv_bfloat16*)x_t, (const __nv_bfloat16*)time_emb,
+                                   suffix_cos, suffix_sin, prefix_mask, v_out, stream);
+  return run_step<__half>(ctx, batch, keys, (const __half*)values, (const __half*)x_t,
+                          (const __half*)time_emb, suffix_cos, suffix_sin, prefix_mask, v_out,
+                          stream);
+}
+
+int pi0_denoise_loop_kv(pi0_ctx* ctx, int batch, const float* keys, const void* values,
+                        const float* x0, const void* time_embs, const float* suffix_cos,
+                        const float* suffix_sin, const float* prefix_mask, float* x_out,
+                        pi0_stream_t stream) {
+  TRY(check_ready(ctx, batch));
+  if (!keys || !values || !x0 || !time_embs || !suffix_cos || !suffix_sin || !prefix_mask || !x_out)
+    return fail(ctx, PI0_ERR_INVALID, "null tensor argument");
+  auto body = [&](cudaStream_t cs) {
+    return is_bf16(ctx)
+               ? run_loop_body<__nv_bfloat16>(ctx, batch, keys, (const __nv_bfloat16*)values, x0,
+                                              (const __nv_bfloat16*)time_embs, suffix_cos,
+                                              suffix_sin, prefix_mask, x_out, cs)
+               : run_loop_body<__half>(ctx, batch, keys, (const __half*)values, x0,
+                                       (const __half*)time_embs, suffix_cos, suffix_sin,
+                                       prefix_mask, x_out, cs);
+  };
+  if (ctx->prof_on) return body(stream);  // eager, so every launch can be timed
+  GraphKey key{batch, {keys, values, x0, time_embs, suffix_cos, suffix_sin, prefix_mask, x_out,
+                       nullptr}};
+  auto it = ctx->graphs.find(key);
+  if (it == ctx->graphs.end()) {
+    cudaStream_t cs = ctx->cap_stream;
+    const int64_t before = ctx->launches;
+    CK(cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal));
+    int r = body(cs);
+    cudaGraph_t graph = nullptr;
+    cudaError_t ce = cudaStreamEndCapture(cs, &graph);
+    const int64_t nodes = ctx->launches - before;
+    ctx->launches = before;
+    if (r) {
+      if (graph) cudaGraphDestroy(graph);
+      return r;
+    }
+    if (ce != cudaSuccess)
+      return fail(ctx, PI0_ERR_CUDA, std::string("capture: ") + cudaGetErrorString(ce));
+    cudaGraphExec_t exec = nullptr;
+    ce = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (ce != cudaSuccess)
+      return fail(ctx, PI0_ERR_CUDA, std::string("instantiate: ") + cudaGetErrorString(ce));
+    if (ctx->graphs.size() > 64) {
+      for (auto& kv : ctx->graphs) cudaGraphExecDestroy(kv.second.first);
+      ctx->graphs.clear();
+    }
+    it = ctx->graphs.emplace(key, std::make_pair(exec, nodes)).first;
+  }
+  CK(cudaGraphLaunch(it->second.first, stream));
+  ctx->launches += it->second.second;
+  return 0;
+}
+
+int pi0_quantize_weight(int quant, int dtype, const void* w, int64_t n_out, int64_t k,
+                        uint32_t* q_weight, void* q_scale, pi0_stream_t stream) {
+  if (!w || !q_weight || !q_scale || n_out < 1 || k < 1) return PI0_ERR_INVALID;
+  if (quant != PI0_QUANT_Q4 && quant != PI0_QUANT_Q3) return PI0_ERR_INVALID;
+  const int G = quant == PI0_QUANT_Q3 ? 40 : 32, bits = quant == PI0_QUANT_Q3 ? 3 : 4;
+  const int epw = quant == PI0_QUANT_Q3 ? 10 : 8, maxint = quant == PI0_QUANT_Q3 ? 3 : 7;
+  int64_t n = n_out * ((k + G - 1) / G);
+  int blocks = (int)((n + 255) / 256);
+  if (dtype == PI0_F16)
+    quantize_kernel<__half><<<blocks, 256, 0, stream>>>((const __half*)w, n_out, k, G, bits, epw,
+                                                         maxint, q_weight, (__half*)q_scale);
+  else if (dtype == PI0_BF16)
+    quantize_kernel<__nv_bfloat16><<<blocks, 256, 0, stream>>>(
+        (const __nv_bfloat16*)w, n_out, k, G, bits, epw, maxint, q_weight, (__nv_bfloat16*)q_scale);
+  else
+    return PI0_ERR_INVALID;
+  return cudaGetLastError() == cudaSuccess ? 0 : PI0_ERR_CUDA;
+}
+
+int pi0_dequantize_weight(int quant, int dtype, const uint32_t* q_weight, const void* q_scale,
+                          int64_t n_out, int64_t k, void* w, pi0_stream_t stream) {
+  if (!w || !q_weight || !q_scale || n_out < 1 || k < 1) return PI0_ERR_INVALID;
+  if (quant != PI0_QUANT_Q4 && quant != PI0_QUANT_Q3) return PI0_ERR_INVALID;
+  const int G = quant == PI0_QUANT_Q3 ? 40 : 32, bits = quant == PI0_QUANT_Q3 ? 3 : 4;
+  const int epw = quant == PI0_QUANT_Q3 ? 10 : 8, maxint = quant == PI0_QUANT_Q3 ? 3 : 7;
+  int64_t n = n_out * k;
+  int blocks = (int)((n + 255) / 256);
+  if (dtype == PI0_F16)
+    dequantize_kernel<__half><<<blocks, 256, 0, stream>>>(q_weight, (const __half*)q_scale, n_out,
+                                                          k, G, bits, epw, maxint, (__half*)w);
+  else if (dtype == PI0_BF16)
+    dequantize_kernel<__nv_bfloat16><<<blocks, 256, 0, stream>>>(
+        q_weight, (const __nv_bfloat16*)q_scale, n_out, k, G, bits, epw, maxint,
+        (__nv_bfloat16*)w);
+  else
+    return PI0_ERR_INVALID;
+  return cudaGetLastError() == cudaSuccess ? 0 : PI0_ERR_CUDA;
+}
+
+int64_t pi0_launch_count(const pi0_ctx* ctx) { return ctx ? ctx->launches : -1; }
+
+int pi0_profile_enable(pi0_ctx* ctx, int on) {
+  if (!ctx) return PI0_ERR_INVALID;
+  CK(cudaSetDevice(ctx->device));
+  for (auto& r : ctx->prof) {
+    ctx->ev_pool.push_back(r.a);
+    ctx->ev_pool.push_back(r.b);
+  }
+  ctx->prof.clear();
+  ctx->prof_on = on != 0;
+  return 0;
+}
+
+int pi0_profile_read(pi0_ctx* ctx, int n_families, int64_t* launches, double* total_ms) {
+  if (!ctx || !launches || !total_ms) return PI0_ERR_INVALID;
+  CK(cudaSetDevice(ctx->device));
+  for (int f = 0; f < n_families; ++f) {
+    launches[f] = 0;
+    total_ms[f] = 0.0;
+  }
+  for (auto& r : ctx->prof) {
+    CK(cudaEventSynchronize(r.b));
+    float ms = 0.f;
+    CK(cudaEventElapsedTime(&ms, r.a, r.b));
+    if (r.fam < n_families) {
+      launches[r.fam] += 1;
+      total_ms[r.fam] += ms;
+    }
+  }
+  return 0;
+}
+
+int pi0_profile_families(void) { return F_NUM; }
+
+const char* pi0_profile_family_name(int family) {
+  return family >= 0 && family < F_NUM ? kFamName[family] : "";
+}
+
+}  // extern "C"

@@ -1,0 +1,3 @@
+"""Version information."""
+
+__version__ = "0.1.0.b200"

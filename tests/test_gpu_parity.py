@@ -1,0 +1,217 @@
+"""GPU parity: libpi0b200 (through its C ABI) against the CPU oracle and the committed fixtures.
+
+Tolerances (the hot-path contract): end outputs cosine ≥ 0.9995 and max-abs ≤ 2e-2 in fp16;
+fp32 K cache within 1e-2 relative of the oracle's; bit-exact where the math is identical by
+construction (in-graph loop vs host-stepped loop).
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import cosine, max_abs
+from gpu_common import Model, config
+from oracle import pi0_oracle as O
+from tests.golden import recipes
+
+pytestmark = pytest.mark.gpu
+
+COS, MAXABS = 0.9995, 2e-2
+
+
+def _np(t):
+    return t.float().cpu().numpy()
+
+
+@pytest.fixture(scope="module")
+def mini():
+    return Model(config(recipes.MINI), max_batch=4)
+
+
+def _check(out, ref, cos=COS, mx=MAXABS, what=""):
+    c, m = cosine(out, ref), max_abs(out, ref)
+    print(f"[parity] {what}: cos={c:.7f} max_abs={m:.3e}")
+    assert c >= cos and m <= mx, (what, c, m)
+
+
+def test_prefill_kv_matches_golden(mini, golden):
+    inp = mini.inputs()
+    pm = O.prefix_mask(mini.cfg.prefix_len)
+    k, v = mini.rt.prefill(inp["prefix"], pm)
+    torch.cuda.synchronize()
+    kr, vr = golden["mini16_keys"], golden["mini16_values"]
+    assert k.shape == kr.shape and k.dtype == torch.float32 and v.dtype == torch.float16
+    _check(_np(k), kr, 0.99999, 1e-2 * np.abs(kr).max(), "prefill keys")
+    _check(_np(v), vr, 0.99999, 1e-2 * np.abs(vr).max(), "prefill values")
+
+
+def test_denoise_step_kv_matches_golden(mini, golden):
+    inp = mini.inputs()
+    cfg = mini.cfg
+    pm = O.prefix_mask(cfg.prefix_len)
+    sc, ss = O.suffix_rope(cfg, cfg.prefix_len)
+    # oracle K/V in (isolates the step), then the full GPU chain
+    v1 = mini.rt.denoise_step_kv(golden["mini16_keys"], golden["mini16_values"], inp["x_t"],
+                                 inp["time_emb"], sc, ss, pm)
+    _check(_np(v1), golden["mini16_v"], what="step on oracle K/V")
+    k, vv = mini.rt.prefill(inp["prefix"], pm)
+    v2 = mini.rt.denoise_step_kv(k, vv, inp["x_t"], inp["time_emb"], sc, ss, pm)
+    assert v2.dtype == torch.float32 and tuple(v2.shape) == (1, cfg.action_horizon, cfg.action_dim)
+    _check(_np(v2), golden["mini16_v"], what="prefill + step")
+
+
+def test_denoise_loop_kv_matches_golden(mini, golden):
+    inp = mini.inputs()
+    cfg = mini.cfg
+    pm = O.prefix_mask(cfg.prefix_len)
+    sc, ss = O.suffix_rope(cfg, cfg.prefix_len)
+    te = O.time_embs(cfg.num_denoise_steps, cfg.action_expert.width)
+    k, v = mini.rt.prefill(inp["prefix"], pm)
+    x = mini.rt.denoise_loop_kv(k, v, inp["noise"], te, sc, ss, pm)
+    _check(_np(x), golden["mini16_loop"], what="loop")
+    # replaying the captured graph with the same arguments gives the same bits
+    x2 = mini.rt.denoise_loop_kv(k, v, inp["noise"], te, sc, ss, pm)
+    assert torch.equal(x, x2)
+
+
+def test_loop_equals_host_stepped_loop_bitwise(mini):
+    """compare_loop (python/mlc_vla/compare_loop.py): in-graph loop == host loop. Both paths run
+    the same kernels on the same inputs, so the bits agree."""
+    inp = mini.inputs(seed=5)
+    cfg = mini.cfg
+    pm = O.prefix_mask(cfg.prefix_len)
+    sc, ss = O.suffix_rope(cfg, cfg.prefix_len)
+    n = cfg.num_denoise_steps
+    te = O.time_embs(n, cfg.action_expert.width)
+    k, v = mini.rt.prefill(inp["prefix"], pm)
+    xg = _np(mini.rt.denoise_loop_kv(k, v, inp["noise"], te, sc, ss, pm))
+    x = inp["noise"].astype(np.float32)
+    for i in range(n):
+        vv = _np(mini.rt.denoise_step_kv(k, v, x.astype(np.float16), te[i:i + 1], sc, ss, pm))
+        x = x + (-1.0 / n) * vv
+    assert cosine(x, xg) >= 0.99999
+    assert np.array_equal(x, xg)
+
+
+def test_batch_of_requests_matches_single(mini):
+    """Independent requests in one call (own prefix, pad mask, RoPE offset) equal B=1 calls."""
+    cfg = mini.cfg
+    b = 3
+    inp = mini.inputs(seed=2, batch=b)
+    nvs = [cfg.prefix_len, cfg.prefix_len - 7, cfg.prefix_len // 2]
+    pm = np.concatenate([O.prefix_mask(cfg.prefix_len, nv) for nv in nvs], 0)
+    rope = [O.suffix_rope(cfg, nv) for nv in nvs]
+    sc = np.concatenate([r[0] for r in rope], 0)
+    ss = np.concatenate([r[1] for r in rope], 0)
+    te = O.time_embs(cfg.num_denoise_steps, cfg.action_expert.width)
+    k, v = mini.rt.prefill(inp["prefix"], pm)
+    xb = _np(mini.rt.denoise_loop_kv(k, v, inp["noise"], te, sc, ss, pm))
+    for i in range(b):
+        k1, v1 = mini.rt.prefill(inp["prefix"][i:i + 1], pm[i:i + 1])
+        np.testing.assert_allclose(_np(k1)[:, 0], _np(k)[:, i], rtol=0, atol=1e-6 * 0 + 2e-3)
+        x1 = _np(mini.rt.denoise_loop_kv(k1, v1, inp["noise"][i:i + 1], te, sc[i:i + 1],
+                                         ss[i:i + 1], pm[i:i + 1]))
+        _check(x1, xb[i:i + 1], 0.99999, 1e-2, f"batch row {i}")
+        # and against the oracle with the same padding
+        ko, vo = mini.oracle_kv(inp["prefix"][i:i + 1], pm[i:i + 1])
+        xo = O.denoise_loop_kv(mini.p, cfg, ko, vo, inp["noise"][i:i + 1], te, sc[i:i + 1],
+                               ss[i:i + 1], pm[i:i + 1])
+        _check(x1, xo, what=f"padded request {i} vs oracle")
+
+
+def test_pad_invariance():
+    """compare_pad (python/mlc_vla/compare_pad.py:62-91) on the GPU: garbage pad tokens that
+    the mask hides do not change v."""
+    import dataclasses
+
+    pad = 5
+    full = config(recipes.MINI)
+    trunc = dataclasses.replace(full, max_token_len=full.max_token_len - pad)
+    mf, mt = Model(full), Model(trunc)
+    P, V = full.prefix_len, trunc.prefix_len
+    rng = np.random.default_rng(0)
+    prefix = (0.02 * rng.standard_normal((1, P, full.vlm.width))).astype(np.float32)
+    prefix[:, V:] = 10.0 * rng.standard_normal((1, pad, full.vlm.width))
+    x_t = np.zeros((1, full.action_horizon, full.action_dim), np.float32)
+    te = O.sinusoidal_time_emb(0.7, full.action_expert.width)
+
+    def run(m, pre):
+        pm = O.prefix_mask(m.cfg.prefix_len, num_valid=V)
+        k, v = m.rt.prefill(pre, pm)
+        sc, ss = O.suffix_rope(m.cfg, V)
+        return _np(m.rt.denoise_step_kv(k, v, x_t, te, sc, ss, pm))
+
+    a, b = run(mf, prefix), run(mt, prefix[:, :V].copy())
+    assert cosine(a, b) >= 0.9999
+
+
+@pytest.mark.parametrize("kw,dtype", [(recipes.DUMMY, "float16"), (recipes.MINI, "bfloat16")])
+def test_other_shapes_and_dtypes_match_oracle(kw, dtype):
+    m = Model(config(kw, dtype))
+    cfg = m.cfg
+    inp = m.inputs()
+    pm = O.prefix_mask(cfg.prefix_len)
+    sc, ss = O.suffix_rope(cfg, cfg.prefix_len)
+    te = O.time_embs(cfg.num_denoise_steps, cfg.action_expert.width)
+    k, v = m.rt.prefill(inp["prefix"], pm)
+    x = _np(m.rt.denoise_loop_kv(k, v, inp["noise"], te, sc, ss, pm))
+    ko, vo = m.oracle_kv(inp["prefix"], pm)
+    xo = O.denoise_loop_kv(m.p, cfg, ko, vo, inp["noise"], te, sc, ss, pm)
+    tol = MAXABS if dtype == "float16" else 8e-2
+    _check(x, xo, 0.999 if dtype == "bfloat16" else COS, tol, f"{kw['paligemma_variant']} {dtype}")
+
+
+def test_full_width_two_layers_matches_oracle():
+    """Every π0.5 width (2048 / 1024, MLP 16384 / 4096, 8 heads × 256, P=968, S=50, D=32) with
+    two layers: prefill K/V, one step and the 10-step loop against the oracle."""
+    m = Model(config(recipes.FULL2))
+    cfg = m.cfg
+    inp = m.inputs()
+    nv = 868  # last 100 prefix positions padded
+    pm = O.prefix_mask(cfg.prefix_len, nv)
+    sc, ss = O.suffix_rope(cfg, nv)
+    k, v = m.rt.prefill(inp["prefix"], pm)
+    ko, vo = m.oracle_kv(inp["prefix"], pm)
+    _check(_np(k), ko, 0.99999, 1e-2 * np.abs(ko).max(), "full-width keys")
+    _check(_np(v), vo, 0.99999, 1e-2 * np.abs(vo).max(), "full-width values")
+    vs = _np(m.rt.denoise_step_kv(k, v, inp["x_t"], inp["time_emb"], sc, ss, pm))
+    vso = O.denoise_step_kv(m.p, cfg, ko, vo, inp["x_t"], inp["time_emb"], sc, ss, pm)
+    _check(vs, vso, what="full-width step")
+    te = O.time_embs(cfg.num_denoise_steps, cfg.action_expert.width)
+    x = _np(m.rt.denoise_loop_kv(k, v, inp["noise"], te, sc, ss, pm))
+    xo = O.denoise_loop_kv(m.p, cfg, ko, vo, inp["noise"], te, sc, ss, pm)
+    _check(x, xo, what="full-width loop")
+
+
+def test_errors_are_raised_not_silent(mini):
+    from mlc_vla._lib import Pi0Error
+
+    cfg = mini.cfg
+    with pytest.raises(ValueError):
+        mini.rt.prefill(np.zeros((5, cfg.prefix_len, cfg.vlm.width), np.float32),
+                        O.prefix_mask(cfg.prefix_len))  # batch 5 > max_batch 4
+    from mlc_vla.runtime import Pi0Runtime
+
+    rt = Pi0Runtime(cfg, device=0)
+    with pytest.raises(Pi0Error, match="set_params"):
+        rt.prefill(np.zeros((1, cfg.prefix_len, cfg.vlm.width), np.float32),
+                   O.prefix_mask(cfg.prefix_len))
+
+
+@pytest.mark.parametrize("preset", ["q4f16_1", "q4bf16_1", "q3f16_1"])
+def test_gpu_quantiser_bit_exact(preset):
+    from mlc_vla.quant import PRESETS
+    from oracle import quant_oracle as Q
+
+    q = PRESETS[preset]
+    rng = np.random.default_rng(3)
+    w = (0.02 * rng.standard_normal((96, 1000))).astype(np.float32)
+    w[5, :40] = 0  # an all-zero group
+    tdt = torch.float16 if q.model_dtype == "float16" else torch.bfloat16
+    wt = torch.from_numpy(w).to("cuda", tdt)
+    qw, qs = q.quantize_weight(wt)
+    oq, os_ = Q.quantize(wt.float().cpu().numpy(), preset)
+    assert np.array_equal(qw.cpu().numpy().view(np.uint32), oq)
+    assert np.array_equal(qs.float().cpu().numpy(), os_)
+    dq = q.dequantize(qw, qs, 1000)
+    assert np.array_equal(dq.float().cpu().numpy(), Q.dequantize(oq, os_, preset, 1000))

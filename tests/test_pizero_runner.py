@@ -1,0 +1,94 @@
+"""GPU: PiZeroRunner contract (port of the reference's python/tests/test_pizero_runner.py, on the
+`cuda` target with float16 instead of the `c` target with float32)."""
+
+import numpy as np
+import pytest
+
+from conftest import cosine
+from tests.golden import recipes
+
+pytestmark = pytest.mark.gpu
+
+DUMMY_KWARGS = dict(recipes.DUMMY, dtype="float16")
+
+
+@pytest.fixture(scope="module")
+def runner():
+    from mlc_vla.model.pi0 import Pi0Config
+    from mlc_vla.sample import PiZeroRunner
+
+    return PiZeroRunner(Pi0Config(**DUMMY_KWARGS), target="cuda")
+
+
+@pytest.fixture
+def loaded(runner):
+    rng = np.random.default_rng(0)
+    arrays = []
+    for _name, p in runner.named_params:
+        shape = [int(s) for s in p.shape]
+        if p.dtype.startswith(("int", "uint")):
+            arrays.append(np.zeros(shape, p.dtype))
+        else:
+            arrays.append((0.02 * rng.standard_normal(shape)).astype(p.dtype))
+    params = runner.to_params(arrays)
+    cfg = runner.config
+    prefix = (0.02 * rng.standard_normal((1, cfg.prefix_len, cfg.vlm.width))).astype("float32")
+    return params, prefix
+
+
+def test_cublas_guard_off(runner):
+    assert runner.cublas is False
+
+
+def test_sample_output_shape_and_finite(runner, loaded):
+    params, prefix = loaded
+    cfg = runner.config
+    out = runner.sample(params, prefix, num_steps=cfg.num_denoise_steps, seed=7)
+    assert out.shape == (1, cfg.action_horizon, cfg.action_dim)
+    assert out.dtype == np.float32
+    assert np.all(np.isfinite(out))
+
+
+def test_sample_graph_matches_host_loop(runner, loaded):
+    params, prefix = loaded
+    cfg = runner.config
+    noise = np.random.default_rng(3).standard_normal(
+        (1, cfg.action_horizon, cfg.action_dim)).astype("float32")
+    host = runner.sample(params, prefix, noise=noise, num_steps=cfg.num_denoise_steps)
+    graph = runner.sample_graph(params, prefix, noise=noise)
+    assert graph.shape == host.shape == (1, cfg.action_horizon, cfg.action_dim)
+    assert cosine(host, graph) >= 0.99999
+
+
+def test_sample_accepts_prefix_pad(runner, loaded):
+    params, prefix = loaded
+    cfg = runner.config
+    pad = np.zeros((cfg.prefix_len,), dtype=np.float32)
+    pad[: cfg.prefix_len // 2] = 1.0
+    out = runner.sample(params, prefix, num_steps=cfg.num_denoise_steps, seed=1, prefix_pad=pad)
+    assert out.shape == (1, cfg.action_horizon, cfg.action_dim)
+    assert np.all(np.isfinite(out))
+
+
+def test_vm_function_contract(runner, loaded):
+    """test_compile_and_run.py: every exported function through the VM-style interface."""
+    from mlc_vla.sample import make_prefix_mask_np, make_rope_np, make_time_embs
+
+    params, prefix = loaded
+    cfg = runner.config
+    vm = runner.vm
+    rng = np.random.default_rng(1)
+    pm = make_prefix_mask_np(cfg.prefix_len)
+    c, s = make_rope_np(cfg.suffix_len, cfg.vlm.head_dim, cfg.rope_theta, offset=cfg.prefix_len)
+    kv = vm["prefill"](prefix.astype(np.float16), pm, params)
+    keys, values = kv[0], kv[1]
+    assert cfg.prefix_len in keys.shape and cfg.vlm.head_dim in keys.shape
+    assert np.all(np.isfinite(keys.numpy())) and np.all(np.isfinite(values.numpy()))
+    x_t = rng.standard_normal((1, cfg.action_horizon, cfg.action_dim)).astype(np.float16)
+    te = rng.standard_normal((1, cfg.action_expert.width)).astype(np.float16)
+    v = vm["denoise_step_kv"](keys, values, x_t, te, c, s, pm, params).numpy()
+    assert v.shape == (1, cfg.action_horizon, cfg.action_dim) and str(v.dtype) == "float32"
+    x0 = rng.standard_normal((1, cfg.action_horizon, cfg.action_dim)).astype(np.float32)
+    tes = np.concatenate(make_time_embs(cfg.num_denoise_steps, cfg.action_expert.width), 0)
+    out = vm["denoise_loop_kv"](keys, values, x0, tes.astype(np.float16), c, s, pm, params).numpy()
+    assert out.shape == (1, cfg.action_horizon, cfg.action_dim) and np.all(np.isfinite(out))
