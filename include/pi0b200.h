@@ -119,7 +119,18 @@ int pi0_quantize_weight(int quant, int dtype, const void* w, int64_t n_out, int6
 int pi0_dequantize_weight(int quant, int dtype, const uint32_t* q_weight, const void* q_scale,
                           int64_t n_out, int64_t k, void* w, pi0_stream_t stream);
 
-/* ---- measurement hooks (no counterpart in the reference; used by bench.py) -------------- */
+/* ---- building block and measurement hooks (no counterpart in the reference) --------------- */
+
+/* y[M, N] = x[M, K] · w[N, K]^T in the context's model dtype (fp32 accumulation, one rounding):
+ * the GEMM engine every projection of the path runs on, exposed for direct tests. engine: 0 =
+ * automatic (tcgen05 for M >= 128), 1 = tcgen05 tensor cores, 2 = warp-level mma. */
+int pi0_linear(pi0_ctx* ctx, const void* x, int M, int K, const void* w, int N, void* y,
+               int engine, pi0_stream_t stream);
+
+/* Reads and clears the device error flag (synchronises the context's device). Nonzero means a
+ * bounded wait inside a kernel gave up. */
+int pi0_device_error(pi0_ctx* ctx);
+
 
 /* Kernels this context has launched so far (a replayed graph counts its kernel nodes). */
 int64_t pi0_launch_count(const pi0_ctx* ctx);

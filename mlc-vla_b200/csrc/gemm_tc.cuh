@@ -1,0 +1,297 @@
+// Blackwell (sm_100a) GEMM on 5th-generation tensor cores:  C[M,N] = A[M,K] · W[N,K]^T with
+// the same fused epilogue functors as the warp-level path (gemm_mma.cuh).
+//
+//   * TMA (cp.async.bulk.tensor, 128-byte swizzle, no multicast) stages 128×64 A tiles and
+//     BN×64 W tiles into a STAGES-deep shared-memory ring guarded by mbarriers;
+//   * one thread issues tcgen05.mma (kind::f16, M=128, N=BN, K=16 per instruction) with the
+//     accumulator in tensor memory; tcgen05.commit releases ring slots and hands finished
+//     accumulators to the epilogue;
+//   * the accumulator is double buffered in TMEM (2·BN columns), so four epilogue warps drain
+//     tile i (tcgen05.ld → registers → functor) while the MMA warp accumulates tile i+1;
+//   * persistent CTAs (one per SM) walk the tiles M-fastest, so the CTAs working at the same
+//     time share W tiles through L2 and every weight byte comes from HBM about once.
+// Every mbarrier wait is bounded (about one second of globaltimer); on timeout the kernel sets
+// *err, leaves its loops, waits for its own tensor-core work and frees TMEM before returning.
+#pragma once
+
+#include <cuda.h>
+
+#include "common.cuh"
+
+namespace pi0 {
+namespace tc {
+
+constexpr int BM = 128;
+constexpr int BK = 64;                       // 64 × 16-bit = one 128-byte swizzle row
+constexpr unsigned long long kTimeoutNs = 1000000000ull;
+
+enum ErrCode { ERR_NONE = 0, ERR_TIMEOUT_PRODUCER = 1, ERR_TIMEOUT_MMA = 2, ERR_TIMEOUT_EPI = 3 };
+
+__device__ __forceinline__ unsigned long long globaltimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Wait for the phase of parity `parity` to complete; false (and *err = code) after ~1 s, or as
+// soon as another role has reported an error (unless `bail` is false: drain waits).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code,
+                                          bool bail = true) {
+  if (mbar_try(bar, parity)) return true;
+  unsigned long long t0 = globaltimer();
+  while (true) {
+    for (int i = 0; i < 64; ++i)
+      if (mbar_try(bar, parity)) return true;
+    if (bail && *(volatile int*)err != 0) return false;
+    if (globaltimer() - t0 > kTimeoutNs) {
+      atomicCAS(err, 0, code);
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                            int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, "
+      "%4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
+}
+
+// Shared-memory matrix descriptor, K-major operand in the 128-byte swizzle layout written by TMA:
+// rows of 128 B, 8-row (1024 B) swizzle atoms, so the stride between 8-row groups is 1024 B.
+__device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFF);     // start address
+  d |= (uint64_t)1 << 16;                      // leading-dimension byte offset (unused here)
+  d |= (uint64_t)(1024 >> 4) << 32;            // stride-dimension byte offset
+  d |= (uint64_t)1 << 46;                      // descriptor version (sm_100)
+  d |= (uint64_t)2 << 61;                      // layout: 128-byte swizzle
+  return d;
+}
+
+// Instruction descriptor of tcgen05.mma kind::f16: fp32 accumulate, A and B of the same 16-bit
+// type (fp16 or bf16), both K-major.
+template <typename T>
+__host__ __device__ constexpr uint32_t idesc_f16(int m, int n) {
+  return (1u << 4)                                  // D format: f32
+         | ((Tr<T>::kBf16 ? 1u : 0u) << 7)          // A format
+         | ((Tr<T>::kBf16 ? 1u : 0u) << 10)         // B format
+         | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
+}
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// 32 lanes × 32 consecutive 32-bit columns: thread i of the warp gets lane (quarter·32 + i).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
+      "%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+template <int BN, int STAGES>
+struct Smem {
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE = A_BYTES + B_BYTES;
+  static constexpr int BYTES = STAGES * STAGE + 1024;  // + alignment slack
+  // double-buffered accumulator, rounded up to the power of two tcgen05.alloc requires
+  static constexpr uint32_t TMEM_COLS = 2 * BN <= 32 ? 32 : 2 * BN <= 64 ? 64 : 2 * BN <= 128 ? 128
+                                        : 2 * BN <= 256 ? 256 : 512;
+};
+
+template <typename T, int BN, int STAGES, class Epi>
+__global__ void __launch_bounds__(192, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   int M, int N, int K, Epi epi, int* err) {
+  using S = Smem<BN, STAGES>;
+  static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN");
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sbase = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                              ~static_cast<uintptr_t>(1023));
+  __shared__ __align__(8) uint64_t full[STAGES], empty[STAGES], tfull[2], tempty[2], drain;
+  __shared__ uint32_t s_tmem;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m_tiles = (M + BM - 1) / BM, n_tiles = (N + BN - 1) / BN;
+  const int tiles = m_tiles * n_tiles;
+  const int nk = (K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 4);
+    }
+    mbar_init(&drain, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(&s_tmem)),
+                 "r"(S::TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s_tmem;
+
+  if (warp == 0) {
+    if (lane == 0) {  // TMA producer
+      int s = 0;
+      uint32_t ph = 0;
+      uint32_t issued = 0;  // bit s: stage s has a load in flight or landed (phase ph_of[s])
+      uint32_t ph_of = 0;
+      for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+        const int m0 = (t % m_tiles) * BM, n0 = (t / m_tiles) * BN;
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(&empty[s], ph ^ 1, err, ERR_TIMEOUT_PRODUCER)) goto producer_done;
+          uint8_t* st = sbase + s * S::STAGE;
+          mbar_expect_tx(&full[s], S::STAGE);
+          tma_load_2d(st, &tmA, &full[s], kb * BK, m0);
+          tma_load_2d(st + S::A_BYTES, &tmB, &full[s], kb * BK, n0);
+          issued |= 1u << s;
+          ph_of = (ph_of & ~(1u << s)) | (ph << s);
+          if (++s == STAGES) {
+            s = 0;
+            ph ^= 1;
+          }
+        }
+      }
+    producer_done:
+      // never leave with a TMA write into this CTA's shared memory still in flight
+      for (int st = 0; st < STAGES; ++st)
+        if (issued & (1u << st))
+          mbar_wait(&full[st], (ph_of >> st) & 1u, err, ERR_TIMEOUT_PRODUCER, false);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {  // MMA issuer
+      constexpr uint32_t idesc = idesc_f16<T>(BM, BN);
+      int s = 0;
+      uint32_t ph = 0;
+      int i = 0;
+      for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++i) {
+        const int acc = i & 1;
+        const uint32_t aph = (i >> 1) & 1;
+        if (!mbar_wait(&tempty[acc], aph ^ 1, err, ERR_TIMEOUT_MMA)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + acc * BN;
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(&full[s], ph, err, ERR_TIMEOUT_MMA)) goto mma_done;
+          tc_fence_after();
+          const uint32_t sa = smem_u32(sbase + s * S::STAGE);
+          const uint64_t da = desc_sw128(sa), db = desc_sw128(sa + S::A_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)  // +32 B per K step inside the swizzle row
+            umma_f16(d, da + 2 * k, db + 2 * k, idesc, (kb | k) != 0);
+          umma_commit(&empty[s]);
+          if (++s == STAGES) {
+            s = 0;
+            ph ^= 1;
+          }
+        }
+        umma_commit(&tfull[acc]);
+      }
+    mma_done:
+      // every issued MMA completes before TMEM is released
+      umma_commit(&drain);
+      mbar_wait(&drain, 0, err, ERR_TIMEOUT_MMA, false);
+    }
+  } else {  // epilogue warps 2..5: TMEM lane quarter = warp % 4
+    const int q = warp & 3;
+    int i = 0;
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++i) {
+      const int acc = i & 1;
+      const uint32_t aph = (i >> 1) & 1;
+      const int m0 = (t % m_tiles) * BM, n0 = (t / m_tiles) * BN;
+      bool ok = true;
+      if (lane == 0) ok = mbar_wait(&tfull[acc], aph, err, ERR_TIMEOUT_EPI);
+      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+      if (!ok) break;
+      tc_fence_after();
+      const int row = m0 + q * 32 + lane;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t v[32];
+        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + acc * BN + c, v);
+        if (row < M) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int col = n0 + c + 2 * j;
+            if (col < N) epi(row, col, __uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]));
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(S::TMEM_COLS));
+  }
+}
+
+}  // namespace tc
+}  // namespace pi0

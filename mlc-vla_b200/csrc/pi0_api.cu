@@ -26,6 +26,7 @@
 #include "attention.cuh"
 #include "common.cuh"
 #include "gemm_mma.cuh"
+#include "gemm_tc.cuh"
 #include "small_kernels.cuh"
 
 using namespace pi0;
@@ -102,7 +103,9 @@ struct pi0_ctx {
   float* splitk_ws = nullptr;
   size_t splitk_floats = 0;
   int* tickets = nullptr;
+  int* dev_err = nullptr;  // device error flag written by bounded waits
   int num_sms = 148;
+  bool use_tc = true;      // tensor-core (tcgen05) GEMMs for M >= 128
 
   cudaStream_t cap_stream = nullptr;
   std::map<GraphKey, std::pair<cudaGraphExec_t, int64_t>> graphs;  // exec, kernel nodes
@@ -267,6 +270,79 @@ int validate(const pi0_config& g, std::string& why) {
 }
 
 
+// ---- TMA tensor maps (driver entry point fetched through the runtime, no libcuda link) ------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn g_encode = nullptr;
+
+int get_encode(pi0_ctx* ctx) {
+  if (g_encode) return 0;
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  CK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q));
+  if (q != cudaDriverEntryPointSuccess || !fn)
+    return fail(ctx, PI0_ERR_CUDA, "cuTensorMapEncodeTiled entry point not found");
+  g_encode = (EncodeTiledFn)fn;
+  return 0;
+}
+
+// 2-D K-major tile map of a [rows, cols] 16-bit matrix with row stride ld (elements):
+// box = 64 columns (128 B, one swizzle row) × box_rows rows, zero fill out of bounds.
+int make_tmap(pi0_ctx* ctx, CUtensorMap* m, const void* base, int rows, int cols, int ld,
+              int box_rows, bool bf16) {
+  TRY(get_encode(ctx));
+  if (((uintptr_t)base & 15) || ((size_t)ld * 2) % 16)
+    return fail(ctx, PI0_ERR_INVALID, "TMA operand must be 16-byte aligned with 16-byte row stride");
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                        2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(ctx, PI0_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+  return 0;
+}
+
+template <typename T, int BN, int ST, class Epi>
+int gemm_tc_launch(pi0_ctx* ctx, const T* A, int lda, const T* W, int ldw, int M, int N, int K,
+                   const Epi& epi, cudaStream_t st, int fam) {
+  CUtensorMap ta, tb;
+  const bool bf = Tr<T>::kBf16;
+  TRY(make_tmap(ctx, &ta, A, M, K, lda, tc::BM, bf));
+  TRY(make_tmap(ctx, &tb, W, N, K, ldw, BN, bf));
+  const int tiles = ((M + tc::BM - 1) / tc::BM) * ((N + BN - 1) / BN);
+  const int grid = std::min(tiles, ctx->num_sms);
+  Prof pr(ctx, fam, st);
+  tc::gemm_tc_kernel<T, BN, ST, Epi><<<grid, 192, tc::Smem<BN, ST>::BYTES, st>>>(ta, tb, M, N, K, epi,
+                                                                             ctx->dev_err);
+  ctx->launches += 1;
+  CKL();
+  return 0;
+}
+
+// Waves-aware tile width for the tensor-core GEMM: the widest of 256 / 160 / 128 whose last
+// wave is fullest.
+int pick_bn(int M, int N, int sms) {
+  const int cands[3] = {256, 160, 128};
+  int best = 128;
+  double best_eff = -1.0;
+  for (int bn : cands) {
+    int tiles = ((M + 127) / 128) * ((N + bn - 1) / bn);
+    int waves = (tiles + sms - 1) / sms;
+    double eff = (double)tiles / (waves * sms) * ((double)N / (((N + bn - 1) / bn) * bn));
+    if (eff > best_eff + 0.02) {
+      best_eff = eff;
+      best = bn;
+    }
+  }
+  return best;
+}
+
 // ---- GEMM launch --------------------------------------------------------------------------
 template <typename T, int BM, int BN, int WM, int WN, int ST, class Epi>
 int gemm_launch_cfg(pi0_ctx* ctx, const T* A, int lda, const T* W, int ldw, int M, int N, int K,
@@ -294,7 +370,14 @@ int gemm_launch_cfg(pi0_ctx* ctx, const T* A, int lda, const T* W, int ldw, int 
 
 template <typename T, class Epi>
 int gemm(pi0_ctx* ctx, const T* A, int lda, const T* W, int ldw, int M, int N, int K,
-         const Epi& epi, cudaStream_t st, int fam) {
+         const Epi& epi, cudaStream_t st, int fam, int engine = 0) {
+  if ((engine == 0 && M >= 128 && ctx->use_tc) || engine == 1) {
+    switch (pick_bn(M, N, ctx->num_sms)) {
+      case 256: return gemm_tc_launch<T, 256, 4>(ctx, A, lda, W, ldw, M, N, K, epi, st, fam);
+      case 160: return gemm_tc_launch<T, 160, 5>(ctx, A, lda, W, ldw, M, N, K, epi, st, fam);
+      default: return gemm_tc_launch<T, 128, 6>(ctx, A, lda, W, ldw, M, N, K, epi, st, fam);
+    }
+  }
   if (M >= 256) {
     return gemm_launch_cfg<T, 128, 128, 64, 32, 4>(ctx, A, lda, W, ldw, M, N, K, epi, 1, st, fam);
   }
@@ -566,10 +649,19 @@ int attr_gemm(pi0_ctx* ctx) {
                           GemmCfg<T, BM, BN, WM, WN, ST>::SMEM));
   return 0;
 }
+template <typename T, int BN, int ST, class Epi>
+int attr_tc(pi0_ctx* ctx) {
+  CK(cudaFuncSetAttribute(tc::gemm_tc_kernel<T, BN, ST, Epi>,
+                          cudaFuncAttributeMaxDynamicSharedMemorySize, tc::Smem<BN, ST>::BYTES));
+  return 0;
+}
 template <typename T, class Epi>
 int attr_gemm_both(pi0_ctx* ctx) {
   TRY((attr_gemm<T, 128, 128, 64, 32, 4, Epi>(ctx)));
   TRY((attr_gemm<T, 64, 64, 32, 32, 4, Epi>(ctx)));
+  TRY((attr_tc<T, 256, 4, Epi>(ctx)));
+  TRY((attr_tc<T, 160, 5, Epi>(ctx)));
+  TRY((attr_tc<T, 128, 6, Epi>(ctx)));
   return 0;
 }
 template <typename T, int HD>
@@ -584,6 +676,7 @@ int setup_attrs(pi0_ctx* ctx) {
   TRY(attr_gemm_both<T, EpiResid<T>>(ctx));
   TRY(attr_gemm_both<T, EpiGatedResid<T>>(ctx));
   TRY(attr_gemm_both<T, EpiGeglu<T>>(ctx));
+  TRY(attr_gemm_both<T, EpiStore<T>>(ctx));
   switch (ctx->cfg.head_dim) {
     case 16: TRY((attr_attn<T, 16>(ctx))); break;
     case 32: TRY((attr_attn<T, 32>(ctx))); break;
@@ -739,6 +832,8 @@ int alloc_all(pi0_ctx* ctx) {
   TRY(dev_alloc(ctx, (void**)&ctx->splitk_ws, ctx->splitk_floats * 4));
   TRY(dev_alloc(ctx, (void**)&ctx->tickets, (1 << 16) * 4));
   CK(cudaMemset(ctx->tickets, 0, (1 << 16) * 4));
+  TRY(dev_alloc(ctx, (void**)&ctx->dev_err, 16));
+  CK(cudaMemset(ctx->dev_err, 0, 16));
   return 0;
 }
 
@@ -1039,6 +1134,32 @@ int pi0_profile_read(pi0_ctx* ctx, int n_families, int64_t* launches, double* to
 }
 
 int pi0_profile_families(void) { return F_NUM; }
+
+int pi0_linear(pi0_ctx* ctx, const void* x, int M, int K, const void* w, int N, void* y,
+               int engine, pi0_stream_t stream) {
+  if (!ctx || !x || !w || !y || M < 1 || N < 2 || K < 8 || (N & 1) || (K % 8))
+    return fail(ctx, PI0_ERR_INVALID, "pi0_linear: need M >= 1, even N, K a multiple of 8");
+  if (engine == 2 && K % 32) return fail(ctx, PI0_ERR_INVALID, "warp-level engine needs K % 32 == 0");
+  CK(cudaSetDevice(ctx->device));
+  if (is_bf16(ctx)) {
+    using T = __nv_bfloat16;
+    return gemm<T>(ctx, (const T*)x, K, (const T*)w, K, M, N, K, EpiStore<T>{(T*)y, N, nullptr},
+                   stream, F_PRE_QKV, engine);
+  }
+  using T = __half;
+  return gemm<T>(ctx, (const T*)x, K, (const T*)w, K, M, N, K, EpiStore<T>{(T*)y, N, nullptr},
+                 stream, F_PRE_QKV, engine);
+}
+
+int pi0_device_error(pi0_ctx* ctx) {
+  if (!ctx) return PI0_ERR_INVALID;
+  CK(cudaSetDevice(ctx->device));
+  CK(cudaDeviceSynchronize());
+  int h = 0;
+  CK(cudaMemcpy(&h, ctx->dev_err, sizeof(int), cudaMemcpyDeviceToHost));
+  CK(cudaMemset(ctx->dev_err, 0, sizeof(int)));
+  return h;
+}
 
 const char* pi0_profile_family_name(int family) {
   return family >= 0 && family < F_NUM ? kFamName[family] : "";

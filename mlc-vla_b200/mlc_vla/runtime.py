@@ -293,6 +293,21 @@ class Pi0Runtime:
         self._hold = (k, v, x, te, sc, ss, m)
         return out
 
+    def linear(self, x: torch.Tensor, w: torch.Tensor, engine: int = 0) -> torch.Tensor:
+        """y = x·wᵀ on the library's GEMM engine (0 auto, 1 tcgen05, 2 warp-level mma)."""
+        x = self._t(x, self.dtype)
+        w = self._t(w, self.dtype)
+        m, k = x.shape
+        n = w.shape[0]
+        y = torch.empty((m, n), dtype=TORCH_DTYPE[self.dtype], device=self.device)
+        _lib.check(self.lib.pi0_linear(self._ctx, x.data_ptr(), m, k, w.data_ptr(), n,
+                                       y.data_ptr(), engine, self._stream()), self._ctx,
+                   "pi0_linear")
+        return y
+
+    def device_error(self) -> int:
+        return int(self.lib.pi0_device_error(self._ctx))
+
     # -- VM-style access --
     def __getitem__(self, name: str):
         if name == "prefill":

@@ -1,0 +1,36 @@
+"""GPU: the GEMM engines (tcgen05/TMA and warp-level mma) against a plain PyTorch fp32 reference
+of the same op, y = round(x·wᵀ), on shapes that exercise partial tiles in M, N and K."""
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def rt():
+    from gpu_common import config
+    from mlc_vla.runtime import Pi0Runtime
+    from tests.golden import recipes
+
+    return Pi0Runtime(config(recipes.MINI), device=0)
+
+
+@pytest.mark.parametrize("engine", [1, 2])
+@pytest.mark.parametrize("m,n,k", [(128, 256, 64), (968, 2560, 2048), (200, 160, 320),
+                                   (50, 1024, 4096), (777, 390, 96), (1000, 32768, 128)])
+def test_linear_matches_torch_fp32(rt, engine, m, n, k):
+    if engine == 2 and k % 32:
+        pytest.skip("warp-level engine needs K % 32 == 0")
+    g = torch.Generator(device="cuda").manual_seed(m * 7 + n + k)
+    x = torch.randn((m, k), generator=g, device="cuda").half()
+    w = (0.05 * torch.randn((n, k), generator=g, device="cuda")).half()
+    y = rt.linear(x, w, engine=engine)
+    torch.cuda.synchronize()
+    assert rt.device_error() == 0
+    ref = (x.float() @ w.float().T)
+    err = (y.float() - ref).abs()
+    tol = 1e-2 * ref.abs().max().item() + 2e-3
+    assert err.max().item() <= tol, (err.max().item(), tol)
+    rel = (err.norm() / ref.norm()).item()
+    assert rel < 2e-3
