@@ -77,7 +77,7 @@ def work_model(cfg, batch):
     w["prefill.down_gemm"] = ((L - 1) * 2 * M0 * W0 * F0, "flop", "tensor")
     w["prefill.rmsnorm"] = ((2 * L - 1) * 2 * M0 * W0 * e, "byte", "hbm")
     nmod = (2 * L + 1) * 3 * W1
-    w["denoise.time_mlp_modulation_gemv"] = ((2 * W1 * W1 + nmod * W1) * e, "byte", "hbm")
+    w["denoise.time_mlp_modulation_gemm"] = ((2 * W1 * W1 + nmod * W1) * e, "byte", "hbm")
     per_step = {
         "denoise.qkv_rope_gemm": L * ((hq + 2 * hkv) * W1 * e + M1 * (W1 * e + hq * 4 + 2 * hkv * 4)),
         "denoise.attention": L * batch * KV * (P + S) * hd * (4 + e),
@@ -305,7 +305,8 @@ def run_b200(args):
         chunk()
     torch.cuda.synchronize(dev)
 
-    # per-kernel-family device times (profiled pass, eager launches bracketed by events)
+    # per-kernel-family device times (profiled pass: the chunk replayed from a captured graph in
+    # which every launch is bracketed by event-record nodes)
     lib.pi0_profile_enable(rt._ctx, 1)
     chunk()
     torch.cuda.synchronize(dev)

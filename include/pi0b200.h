@@ -123,7 +123,8 @@ int pi0_dequantize_weight(int quant, int dtype, const uint32_t* q_weight, const 
 
 /* y[M, N] = x[M, K] · w[N, K]^T in the context's model dtype (fp32 accumulation, one rounding):
  * the GEMM engine every projection of the path runs on, exposed for direct tests. engine: 0 =
- * automatic (tcgen05 for M >= 128), 1 = tcgen05 tensor cores, 2 = warp-level mma. */
+ * automatic, 1 = tcgen05 tiles (M >= 128), 2 = warp-level mma, 3 = tcgen05 weight-streaming
+ * split-K (M <= 128). */
 int pi0_linear(pi0_ctx* ctx, const void* x, int M, int K, const void* w, int N, void* y,
                int engine, pi0_stream_t stream);
 
@@ -135,9 +136,9 @@ int pi0_device_error(pi0_ctx* ctx);
 /* Kernels this context has launched so far (a replayed graph counts its kernel nodes). */
 int64_t pi0_launch_count(const pi0_ctx* ctx);
 
-/* While enabled, every kernel launch is bracketed by CUDA events on its stream and
- * denoise_loop_kv runs without graph capture, so per-kernel-family device times can be read
- * back. Enabling clears earlier records. */
+/* While enabled, every kernel launch is bracketed by CUDA events, and each call is captured into
+ * a one-shot graph, replayed and synchronised, so per-kernel-family device times (without host
+ * launch gaps) can be read back. Enabling clears earlier records. */
 int pi0_profile_enable(pi0_ctx* ctx, int on);
 /* Synchronises the recorded events and returns, per kernel family (index < pi0_profile_families),
  * its launch count and total device milliseconds. */

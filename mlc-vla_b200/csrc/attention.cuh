@@ -12,8 +12,11 @@
 //
 // Rows of one CTA tile are (t, g) pairs of one kv head: row j -> t = j / G, head = kvh·G + j % G
 // with G = H / KV, so every row of a tile shares the tile's K/V (MQA: all heads of a token).
-// gridDim = (row tiles, key splits, B·KV). With one split the kernel writes the normalised
-// output; with several it writes (m, l, unnormalised O) partials that attn_combine merges.
+// gridDim = (row tiles, key splits, B·KV). K/V tiles of 32 keys are double buffered with
+// cp.async; tiles of cached prefix keys do not depend on the previous kernel and are requested
+// before griddepcontrol.wait. With several key splits the CTAs of one row tile form a cluster
+// and merge their (m, l, O) partials through distributed shared memory in rank order, so no
+// separate combine kernel runs.
 #pragma once
 
 #include "common.cuh"
@@ -33,49 +36,123 @@ struct AttnArgs {
   int Tq, H, KV;
   int keys_per_split;  // multiple of ATT_BK
   T* out;              // [B, Tq, H·hd]
-  float* part_o;       // [B·KV, rows, splits, hd]
-  float* part_ml;      // [B·KV, rows, splits, 2]
+  int a_is_ready;      // segment A was written before the previous kernel (the prefix cache
+                       // during denoise): its tiles may be requested before griddepcontrol.wait
 };
 
 constexpr int ATT_BQ = 64;   // query rows per CTA (4 warps × 16)
-constexpr int ATT_BK = 32;   // keys per iteration
+constexpr int ATT_BK = 32;   // keys per tile
 
 template <int HD>
 struct AttnSmem {
   static constexpr int QLD = HD + 4;   // fp32 row stride (conflict-free tf32 fragment loads)
   static constexpr int KLD = HD + 4;
   static constexpr int VLD = HD + 8;   // 16-bit row stride (conflict-free ldmatrix.trans)
-  static constexpr int BYTES = (ATT_BQ * QLD + ATT_BK * KLD) * 4 + ATT_BK * VLD * 2 + ATT_BK * 4;
+  static constexpr int Q_BYTES = ATT_BQ * QLD * 4;
+  static constexpr int K_BYTES = ATT_BK * KLD * 4;
+  static constexpr int V_BYTES = ATT_BK * VLD * 2;
+  static constexpr int STAGE = K_BYTES + V_BYTES + ATT_BK * 4;
+  static constexpr int BYTES = Q_BYTES + 2 * STAGE;
+  // after the key loop: partial O [64][HD + 4] fp32 and (m, l) [64][2] reuse the same space
+  static constexpr int OLD = HD + 4;
+  static_assert(ATT_BQ * OLD * 4 + ATT_BQ * 8 <= BYTES, "combine buffer");
 };
+
+__device__ __forceinline__ uint32_t attn_cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void attn_cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
+}
+__device__ __forceinline__ uint32_t attn_map(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ float2 attn_ld2(uint32_t addr) {
+  float2 v;
+  asm volatile("ld.shared::cluster.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(addr) : "memory");
+  return v;
+}
 
 template <typename T, int HD>
 __global__ void __launch_bounds__(128) attn_kernel(AttnArgs<T> a) {
   using SM = AttnSmem<HD>;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   float* sQ = reinterpret_cast<float*>(smem_raw);
-  float* sK = sQ + ATT_BQ * SM::QLD;
-  T* sV = reinterpret_cast<T*>(sK + ATT_BK * SM::KLD);
-  float* sMask = reinterpret_cast<float*>(sV + ATT_BK * SM::VLD);
+  auto sK = [&](int s) { return reinterpret_cast<float*>(smem_raw + SM::Q_BYTES + s * SM::STAGE); };
+  auto sV = [&](int s) {
+    return reinterpret_cast<T*>(smem_raw + SM::Q_BYTES + s * SM::STAGE + SM::K_BYTES);
+  };
+  auto sMask = [&](int s) {
+    return reinterpret_cast<float*>(smem_raw + SM::Q_BYTES + s * SM::STAGE + SM::K_BYTES + SM::V_BYTES);
+  };
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int G = a.H / a.KV;
   const int rows = a.Tq * G;
   const int bk = blockIdx.z, b = bk / a.KV, kvh = bk % a.KV;
   const int row0 = blockIdx.x * ATT_BQ;
-  const int split = blockIdx.y, nsplit = gridDim.y;
+  const int nsplit = gridDim.y;
+  const int split = blockIdx.y;
   const int Ltot = a.LA + a.LB;
   const int kbeg = split * a.keys_per_split;
   const int kend = min(Ltot, kbeg + a.keys_per_split);
+  const int ntiles = max(0, (kend - kbeg + ATT_BK - 1) / ATT_BK);
 
-  // Q tile
+  const float* kA = a.kA + ((size_t)b * a.KV + kvh) * a.LA * HD;
+  const T* vA = a.vA + ((size_t)b * a.KV + kvh) * a.LA * HD;
+  const float* kB = a.kB ? a.kB + ((size_t)b * a.KV + kvh) * a.LB * HD : nullptr;
+  const T* vB = a.vB ? a.vB + ((size_t)b * a.KV + kvh) * a.LB * HD : nullptr;
+  const float* mA = a.maskA ? a.maskA + (size_t)b * a.LA : nullptr;
+
+  // K/V tile of keys [k0, k0 + 32) into stage s (zero-filled past kend)
+  auto load_tile = [&](int s, int k0) {
+    float* dk = sK(s);
+    T* dv = sV(s);
+    for (int i = tid; i < ATT_BK * (HD / 4); i += 128) {
+      const int r = i / (HD / 4), ch = i % (HD / 4);
+      const int key = k0 + r;
+      const bool ok = key < kend;
+      const float* src = ok ? (key < a.LA ? kA + (size_t)key * HD : kB + (size_t)(key - a.LA) * HD) : kA;
+      cp_async16(dk + r * SM::KLD + ch * 4, src + (ok ? ch * 4 : 0), ok ? 16 : 0);
+    }
+    for (int i = tid; i < ATT_BK * (HD / 8); i += 128) {
+      const int r = i / (HD / 8), ch = i % (HD / 8);
+      const int key = k0 + r;
+      const bool ok = key < kend;
+      const T* src = ok ? (key < a.LA ? vA + (size_t)key * HD : vB + (size_t)(key - a.LA) * HD) : vA;
+      cp_async16(dv + r * SM::VLD + ch * 8, src + (ok ? ch * 8 : 0), ok ? 16 : 0);
+    }
+    if (tid < ATT_BK) {
+      const int key = k0 + tid;
+      float mv;
+      if (key >= kend) mv = -1e30f;                   // outside this split: contributes 0
+      else if (key < a.LA) mv = mA ? mA[key] : 0.f;    // prefix pad mask
+      else mv = 0.f;                                   // suffix keys are always visible
+      sMask(s)[tid] = mv;
+    }
+  };
+
+  // tiles made only of cached prefix keys (and their mask) are independent of the previous
+  // kernel: start the first one before waiting on it
+  const bool t0_independent = a.a_is_ready && ntiles > 0 && kbeg + ATT_BK <= a.LA;
+  if (t0_independent) load_tile(0, kbeg);
+  cp_async_commit();
+  pdl_trigger();
+  pdl_wait();
+  if (ntiles > 0 && !t0_independent) load_tile(0, kbeg);
+  // Q tile (written by the q/k/v projection)
   for (int i = tid; i < ATT_BQ * (HD / 4); i += 128) {
-    int r = i / (HD / 4), ch = i % (HD / 4);
-    int j = row0 + r;
+    const int r = i / (HD / 4), ch = i % (HD / 4);
+    const int j = row0 + r;
     float* dst = sQ + r * SM::QLD + ch * 4;
     if (j < rows) {
-      int t = j / G, h = kvh * G + (j - t * G);
-      const float* src = a.q + (((size_t)b * a.Tq + t) * a.H + h) * HD + ch * 4;
-      cp_async16(dst, src, 16);
+      const int t = j / G, h = kvh * G + (j - t * G);
+      cp_async16(dst, a.q + (((size_t)b * a.Tq + t) * a.H + h) * HD + ch * 4, 16);
     } else {
       *reinterpret_cast<float4*>(dst) = make_float4(0.f, 0.f, 0.f, 0.f);
     }
@@ -88,44 +165,20 @@ __global__ void __launch_bounds__(128) attn_kernel(AttnArgs<T> a) {
   for (int i = 0; i < HD / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
   float m_r[2] = {-1e30f, -1e30f}, l_r[2] = {0.f, 0.f};
 
-  const float* kA = a.kA + ((size_t)b * a.KV + kvh) * a.LA * HD;
-  const T* vA = a.vA + ((size_t)b * a.KV + kvh) * a.LA * HD;
-  const float* kB = a.kB ? a.kB + ((size_t)b * a.KV + kvh) * a.LB * HD : nullptr;
-  const T* vB = a.vB ? a.vB + ((size_t)b * a.KV + kvh) * a.LB * HD : nullptr;
-  const float* mA = a.maskA ? a.maskA + (size_t)b * a.LA : nullptr;
-
-  for (int k0 = kbeg; k0 < kend; k0 += ATT_BK) {
-    __syncthreads();  // previous tile fully consumed
-    for (int i = tid; i < ATT_BK * (HD / 4); i += 128) {
-      int r = i / (HD / 4), ch = i % (HD / 4);
-      int key = k0 + r;
-      const float* src = key < a.LA ? kA + (size_t)key * HD : kB + (size_t)(key - a.LA) * HD;
-      bool ok = key < kend;
-      cp_async16(sK + r * SM::KLD + ch * 4, ok ? src + ch * 4 : a.q, ok ? 16 : 0);
-    }
-    for (int i = tid; i < ATT_BK * (HD / 8); i += 128) {
-      int r = i / (HD / 8), ch = i % (HD / 8);
-      int key = k0 + r;
-      const T* src = key < a.LA ? vA + (size_t)key * HD : vB + (size_t)(key - a.LA) * HD;
-      bool ok = key < kend;
-      cp_async16(sV + r * SM::VLD + ch * 8, ok ? src + ch * 8 : (const T*)a.q, ok ? 16 : 0);
-    }
-    if (tid < ATT_BK) {
-      int key = k0 + tid;
-      float mv;
-      if (key >= kend) mv = -1e30f;                 // outside this split: contributes 0
-      else if (key < a.LA) mv = mA ? mA[key] : 0.f;  // prefix pad mask
-      else mv = 0.f;                                 // suffix keys are always visible
-      sMask[tid] = mv;
-    }
+  for (int t = 0; t < ntiles; ++t) {
+    const int s = t & 1;
+    if (t + 1 < ntiles) load_tile(s ^ 1, kbeg + (t + 1) * ATT_BK);  // prefetch the next tile
     cp_async_commit();
-    cp_async_wait<0>();
+    cp_async_wait<1>();  // everything but the just-issued prefetch has landed
     __syncthreads();
+    const float* kt = sK(s);
+    const T* vt = sV(s);
+    const float* mt = sMask(s);
 
     // S = Q K^T for this warp's 16 rows × 32 keys
-    float s[4][4];
+    float sc[4][4];
 #pragma unroll
-    for (int n = 0; n < 4; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
+    for (int n = 0; n < 4; ++n) sc[n][0] = sc[n][1] = sc[n][2] = sc[n][3] = 0.f;
     const float* qw = sQ + (warp * 16) * SM::QLD;
 #pragma unroll 4
     for (int kk = 0; kk < HD; kk += 8) {
@@ -137,22 +190,22 @@ __global__ void __launch_bounds__(128) attn_kernel(AttnArgs<T> a) {
 #pragma unroll
       for (int n = 0; n < 4; ++n) {
         uint32_t bf[2];
-        bf[0] = to_tf32(sK[(n * 8 + gq) * SM::KLD + kk + tq]);
-        bf[1] = to_tf32(sK[(n * 8 + gq) * SM::KLD + kk + tq + 4]);
-        mma1688_tf32(s[n], af, bf);
+        bf[0] = to_tf32(kt[(n * 8 + gq) * SM::KLD + kk + tq]);
+        bf[1] = to_tf32(kt[(n * 8 + gq) * SM::KLD + kk + tq + 4]);
+        mma1688_tf32(sc[n], af, bf);
       }
     }
     // mask, online softmax
     float mx[2] = {m_r[0], m_r[1]};
 #pragma unroll
     for (int n = 0; n < 4; ++n) {
-      float mk0 = sMask[n * 8 + tq * 2], mk1 = sMask[n * 8 + tq * 2 + 1];
-      s[n][0] += mk0;
-      s[n][1] += mk1;
-      s[n][2] += mk0;
-      s[n][3] += mk1;
-      mx[0] = fmaxf(mx[0], fmaxf(s[n][0], s[n][1]));
-      mx[1] = fmaxf(mx[1], fmaxf(s[n][2], s[n][3]));
+      const float mk0 = mt[n * 8 + tq * 2], mk1 = mt[n * 8 + tq * 2 + 1];
+      sc[n][0] += mk0;
+      sc[n][1] += mk1;
+      sc[n][2] += mk0;
+      sc[n][3] += mk1;
+      mx[0] = fmaxf(mx[0], fmaxf(sc[n][0], sc[n][1]));
+      mx[1] = fmaxf(mx[1], fmaxf(sc[n][2], sc[n][3]));
     }
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
@@ -165,13 +218,13 @@ __global__ void __launch_bounds__(128) attn_kernel(AttnArgs<T> a) {
     uint32_t pf[2][4];  // P as two m16n8k16 A fragments (keys 0-15, 16-31)
 #pragma unroll
     for (int n = 0; n < 4; ++n) {
-      float p0 = expf(s[n][0] - mx[0]), p1 = expf(s[n][1] - mx[0]);
-      float p2 = expf(s[n][2] - mx[1]), p3 = expf(s[n][3] - mx[1]);
+      const float p0 = expf(sc[n][0] - mx[0]), p1 = expf(sc[n][1] - mx[0]);
+      const float p2 = expf(sc[n][2] - mx[1]), p3 = expf(sc[n][3] - mx[1]);
       rs[0] += p0 + p1;
       rs[1] += p2 + p3;
-      int kt = n >> 1, hi = n & 1;
-      pf[kt][hi * 2 + 0] = Tr<T>::pack(p0, p1);
-      pf[kt][hi * 2 + 1] = Tr<T>::pack(p2, p3);
+      const int kt2 = n >> 1, hi = n & 1;
+      pf[kt2][hi * 2 + 0] = Tr<T>::pack(p0, p1);
+      pf[kt2][hi * 2 + 1] = Tr<T>::pack(p2, p3);
     }
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
@@ -189,75 +242,108 @@ __global__ void __launch_bounds__(128) attn_kernel(AttnArgs<T> a) {
     }
     // O += P V
 #pragma unroll
-    for (int kt = 0; kt < 2; ++kt) {
+    for (int kt2 = 0; kt2 < 2; ++kt2) {
 #pragma unroll
       for (int i = 0; i < HD / 8; i += 2) {
         uint32_t b0, b1, b2, b3;
-        const T* p = sV + (kt * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * SM::VLD + i * 8 +
+        const T* p = vt + (kt2 * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * SM::VLD + i * 8 +
                      (lane >> 4) * 8;
         ldsm_x4_t(b0, b1, b2, b3, p);
         uint32_t bb0[2] = {b0, b1}, bb1[2] = {b2, b3};
-        mma16816<T>(o[i], pf[kt], bb0);
-        mma16816<T>(o[i + 1], pf[kt], bb1);
+        mma16816<T>(o[i], pf[kt2], bb0);
+        mma16816<T>(o[i + 1], pf[kt2], bb1);
       }
     }
+    __syncthreads();  // this stage is refilled two tiles later
   }
+  cp_async_wait<0>();
 
-  // write out
+  if (nsplit == 1) {
 #pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    int j = row0 + warp * 16 + gq + h * 8;
-    if (j >= rows) continue;
-    int t = j / G, head = kvh * G + (j - t * G);
-    if (nsplit == 1) {
-      float inv = 1.f / l_r[h];
+    for (int h = 0; h < 2; ++h) {
+      const int j = row0 + warp * 16 + gq + h * 8;
+      if (j >= rows) continue;
+      const int t = j / G, head = kvh * G + (j - t * G);
+      const float inv = 1.f / l_r[h];
       T* dst = a.out + ((size_t)b * a.Tq + t) * a.H * HD + (size_t)head * HD;
 #pragma unroll
       for (int i = 0; i < HD / 8; ++i) {
-        int d = i * 8 + tq * 2;
-        *reinterpret_cast<uint32_t*>(dst + d) =
-            Tr<T>::pack(o[i][2 * h] * inv, o[i][2 * h + 1] * inv);
-      }
-    } else {
-      size_t base = ((size_t)bk * rows + j) * nsplit + split;
-      float* dst = a.part_o + base * HD;
-#pragma unroll
-      for (int i = 0; i < HD / 8; ++i) {
-        int d = i * 8 + tq * 2;
-        *reinterpret_cast<float2*>(dst + d) = make_float2(o[i][2 * h], o[i][2 * h + 1]);
-      }
-      if (tq == 0) {
-        a.part_ml[base * 2 + 0] = m_r[h];
-        a.part_ml[base * 2 + 1] = l_r[h];
+        const int d = i * 8 + tq * 2;
+        *reinterpret_cast<uint32_t*>(dst + d) = Tr<T>::pack(o[i][2 * h] * inv, o[i][2 * h + 1] * inv);
       }
     }
+    return;
   }
-}
 
-// Merge split partials: O = Σ_s e^{m_s - M} O_s / Σ_s e^{m_s - M} l_s, rounded to the model dtype.
-// grid (rows, B·KV), block hd/2 threads (2 dims each).
-template <typename T>
-__global__ void attn_combine_kernel(AttnArgs<T> a, int hd, int nsplit) {
-  const int G = a.H / a.KV, rows = a.Tq * G;
-  const int j = blockIdx.x, bk = blockIdx.y, b = bk / a.KV, kvh = bk % a.KV;
-  const size_t base = ((size_t)bk * rows + j) * nsplit;
-  float M = -1e30f;
-  for (int s = 0; s < nsplit; ++s) M = fmaxf(M, a.part_ml[(base + s) * 2]);
-  float L = 0.f;
-  for (int s = 0; s < nsplit; ++s) L += expf(a.part_ml[(base + s) * 2] - M) * a.part_ml[(base + s) * 2 + 1];
-  const float inv = 1.f / L;
-  const int t = j / G, head = kvh * G + (j - t * G);
-  T* dst = a.out + ((size_t)b * a.Tq + t) * a.H * hd + (size_t)head * hd;
-  for (int d = threadIdx.x * 2; d < hd; d += blockDim.x * 2) {
-    float o0 = 0.f, o1 = 0.f;
-    for (int s = 0; s < nsplit; ++s) {
-      float w = expf(a.part_ml[(base + s) * 2] - M);
-      float2 v = *reinterpret_cast<const float2*>(a.part_o + (base + s) * hd + d);
-      o0 += w * v.x;
-      o1 += w * v.y;
+  // ---- merge the key splits of this row tile (cluster along grid.y) ----
+  __syncthreads();
+  float* sO = reinterpret_cast<float*>(smem_raw);            // [64][OLD] unnormalised O
+  float* sML = sO + ATT_BQ * SM::OLD;                          // [64][2] (m, l)
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int r = warp * 16 + gq + h * 8;
+#pragma unroll
+    for (int i = 0; i < HD / 8; ++i)
+      *reinterpret_cast<float2*>(sO + r * SM::OLD + i * 8 + tq * 2) = make_float2(o[i][2 * h], o[i][2 * h + 1]);
+    if (tq == 0) {
+      sML[r * 2 + 0] = m_r[h];
+      sML[r * 2 + 1] = l_r[h];
     }
-    *reinterpret_cast<uint32_t*>(dst + d) = Tr<T>::pack(o0 * inv, o1 * inv);
   }
+  attn_cluster_sync();
+  // rank r finishes rows [r·RPR, (r+1)·RPR) of the tile from every rank's partial, in rank order
+  const uint32_t rank = attn_cluster_rank();
+  const int rpr = ATT_BQ / nsplit;
+  const uint32_t oaddr = smem_u32(sO), maddr = smem_u32(sML);
+  __shared__ float s_w[ATT_BQ][16];
+  __shared__ float s_inv[ATT_BQ];
+  if (tid < rpr) {
+    const int r = rank * rpr + tid;
+    float mm[16], ll[16];
+#pragma unroll
+    for (int c = 0; c < 16; ++c)
+      if (c < nsplit) {
+        const float2 ml = attn_ld2(attn_map(maddr + r * 8, c));
+        mm[c] = ml.x;
+        ll[c] = ml.y;
+      }
+    float M = -1e30f;
+#pragma unroll
+    for (int c = 0; c < 16; ++c)
+      if (c < nsplit) M = fmaxf(M, mm[c]);
+    float L = 0.f;
+#pragma unroll
+    for (int c = 0; c < 16; ++c)
+      if (c < nsplit) {
+        const float w = expf(mm[c] - M);
+        s_w[tid][c] = w;
+        L += w * ll[c];
+      }
+    s_inv[tid] = 1.f / L;
+  }
+  __syncthreads();
+  for (int it = tid; it < rpr * (HD / 2); it += 128) {
+    const int rr = it / (HD / 2), d = (it % (HD / 2)) * 2;
+    const int r = rank * rpr + rr;
+    const int j = row0 + r;
+    float2 pv[16];
+#pragma unroll
+    for (int c = 0; c < 16; ++c)
+      if (c < nsplit) pv[c] = attn_ld2(attn_map(oaddr + (r * SM::OLD + d) * 4, c));
+    float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+    for (int c = 0; c < 16; ++c)
+      if (c < nsplit) {
+        s0 += s_w[rr][c] * pv[c].x;
+        s1 += s_w[rr][c] * pv[c].y;
+      }
+    if (j < rows) {
+      const int t = j / G, head = kvh * G + (j - t * G);
+      T* dst = a.out + ((size_t)b * a.Tq + t) * a.H * HD + (size_t)head * HD;
+      *reinterpret_cast<uint32_t*>(dst + d) = Tr<T>::pack(s0 * s_inv[rr], s1 * s_inv[rr]);
+    }
+  }
+  attn_cluster_sync();  // peers may still read this CTA's partial
 }
 
 }  // namespace pi0

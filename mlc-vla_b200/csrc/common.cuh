@@ -112,6 +112,16 @@ __device__ __forceinline__ void mma1688_tf32(float* c, const uint32_t* a, const 
 }
 
 // ------------------------------------------------------------------------------------------
+// programmatic dependent launch: every kernel of the chain waits for its predecessor's results
+// with griddepcontrol.wait before touching them (a no-op when launched without the attribute)
+// and lets its own dependents get scheduled early.
+// ------------------------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// ------------------------------------------------------------------------------------------
 // math
 // ------------------------------------------------------------------------------------------
 // GELU, tanh approximation: 0.5·x·(1 + tanh(√(2/π)·(x + 0.044715·x³))), fp32.

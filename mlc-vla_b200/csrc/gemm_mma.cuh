@@ -27,16 +27,23 @@ struct GemmArgs {
 
 // ---- epilogues: operator()(row, col, v(col), v(col+1)); col is even ----
 
+// y = round(round(acc) + bias) (nn.Linear: matmul, then bias add; bias optional), then
+// optionally round(silu(y)) (the time MLP, pi0_model.py:106-109), stored in the model dtype.
 template <typename T>
-struct EpiStore {  // y = round(round(acc) + bias) (bias optional), stored in the model dtype
+struct EpiStore {
   T* out;
   int ldo;
   const T* bias;
+  int silu = 0;
   __device__ void operator()(int r, int c, float v0, float v1) const {
     float a = Tr<T>::r(v0), b = Tr<T>::r(v1);
     if (bias) {
-      a = a + Tr<T>::f(bias[c]);
-      b = b + Tr<T>::f(bias[c + 1]);
+      a = Tr<T>::r(a + Tr<T>::f(bias[c]));
+      b = Tr<T>::r(b + Tr<T>::f(bias[c + 1]));
+    }
+    if (silu) {
+      a = silu_f(a);
+      b = silu_f(b);
     }
     *reinterpret_cast<uint32_t*>(out + (size_t)r * ldo + c) = Tr<T>::pack(a, b);
   }
@@ -61,12 +68,14 @@ struct EpiGatedResid {  // suffix residual (gemma_dual.py:91-94): x = round(x + 
   const T* gate;      // [rows_per_gate_group ...]: gate[(r / rows_per_gate) * gate_stride + c]
   int rows_per_gate;  // rows that share one gate vector (S·B when the time is shared)
   int gate_stride;
-  __device__ void operator()(int r, int c, float v0, float v1) const {
+  // returns the new (rounded) x values, from which the next norm's Σx² partials are formed
+  __device__ float2 operator()(int r, int c, float v0, float v1) const {
     const T* g = gate + (size_t)(r / rows_per_gate) * gate_stride + c;
     T* p = x + (size_t)r * ldx + c;
-    float a = Tr<T>::f(p[0]) + Tr<T>::r(Tr<T>::r(v0) * Tr<T>::f(g[0]));
-    float b = Tr<T>::f(p[1]) + Tr<T>::r(Tr<T>::r(v1) * Tr<T>::f(g[1]));
+    float a = Tr<T>::r(Tr<T>::f(p[0]) + Tr<T>::r(Tr<T>::r(v0) * Tr<T>::f(g[0])));
+    float b = Tr<T>::r(Tr<T>::f(p[1]) + Tr<T>::r(Tr<T>::r(v1) * Tr<T>::f(g[1])));
     *reinterpret_cast<uint32_t*>(p) = Tr<T>::pack(a, b);
+    return make_float2(a, b);
   }
 };
 
@@ -152,6 +161,8 @@ __global__ void __launch_bounds__(GemmCfg<T, BM, BN, WM, WN, STAGES>::NT)
   T* sA = reinterpret_cast<T*>(smem_raw);
   T* sB = sA + STAGES * BM * C::LDS;
   __shared__ int s_last;
+  pdl_wait();
+  pdl_trigger();
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int wm = warp / C::WARPS_N, wn = warp % C::WARPS_N;

@@ -55,18 +55,21 @@ __device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 // Wait for the phase of parity `parity` to complete; false (and *err = code) after ~1 s, or as
-// soon as another role has reported an error (unless `bail` is false: drain waits).
+// soon as another role has reported an error (unless `bail` is false: drain waits). The hot
+// loop only polls the barrier; the clock is read every 128 polls and the (global) error flag
+// every 8192, so a completed phase is seen without a memory round trip in the way.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code,
                                           bool bail = true) {
   if (mbar_try(bar, parity)) return true;
-  unsigned long long t0 = globaltimer();
-  while (true) {
-    for (int i = 0; i < 64; ++i)
-      if (mbar_try(bar, parity)) return true;
-    if (bail && *(volatile int*)err != 0) return false;
-    if (globaltimer() - t0 > kTimeoutNs) {
-      atomicCAS(err, 0, code);
-      return false;
+  const unsigned long long t0 = globaltimer();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try(bar, parity)) return true;
+    if ((it & 127) == 0) {
+      if (globaltimer() - t0 > kTimeoutNs) {
+        atomicCAS(err, 0, code);
+        return false;
+      }
+      if (bail && (it & 8191) == 0 && *(volatile int*)err != 0) return false;
     }
   }
 }
@@ -191,6 +194,8 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = s_tmem;
+  pdl_wait();
+  pdl_trigger();
 
   if (warp == 0) {
     if (lane == 0) {  // TMA producer

@@ -27,6 +27,7 @@
 #include "common.cuh"
 #include "gemm_mma.cuh"
 #include "gemm_tc.cuh"
+#include "gemm_skinny.cuh"
 #include "small_kernels.cuh"
 
 using namespace pi0;
@@ -58,6 +59,8 @@ struct LayerW {
   void* d;     // [W, F]
   void* ln_in;
   void* ln_post;
+  // action expert only: the same matrices packed for the weight-streaming GEMM
+  void *qkv_p = nullptr, *o_p = nullptr, *gu_p = nullptr, *d_p = nullptr;
 };
 
 struct GraphKey {
@@ -86,6 +89,9 @@ struct pi0_ctx {
   void *mod_w = nullptr, *mod_b = nullptr;
   void *ain_w = nullptr, *ain_b = nullptr, *aout_w = nullptr, *aout_b = nullptr;
   void *tin_w = nullptr, *tin_b = nullptr, *tout_w = nullptr, *tout_b = nullptr;
+  void *mod_w_p = nullptr, *tin_p = nullptr, *tout_p = nullptr;  // packed copies
+  float* ssq = nullptr;  // [max_batch·S][ssq_parts] row Σx² partials of the suffix stream
+  int ssq_parts = 1;
   int* perm_q = nullptr;   // RoPE row permutation of a q block (H·hd rows)
   int* perm_k = nullptr;   // ... of a k block (KV·hd rows)
   int* perm_gu0 = nullptr; // gate/up interleave for F0
@@ -99,13 +105,13 @@ struct pi0_ctx {
   void *xs = nullptr, *xsn = nullptr, *attn_s = nullptr, *hs = nullptr, *vsuf = nullptr;
   float *qs = nullptr, *ksuf = nullptr;
   void *t1 = nullptr, *cond = nullptr, *mods = nullptr;
-  float *part_o = nullptr, *part_ml = nullptr;
   float* splitk_ws = nullptr;
   size_t splitk_floats = 0;
   int* tickets = nullptr;
   int* dev_err = nullptr;  // device error flag written by bounded waits
   int num_sms = 148;
   bool use_tc = true;      // tensor-core (tcgen05) GEMMs for M >= 128
+  bool pdl = true;         // programmatic dependent launch between the kernels of a chain
 
   cudaStream_t cap_stream = nullptr;
   std::map<GraphKey, std::pair<cudaGraphExec_t, int64_t>> graphs;  // exec, kernel nodes
@@ -134,7 +140,7 @@ enum Fam {
 const char* kFamName[F_NUM] = {
   "prefill.rmsnorm", "prefill.qkv_rope_gemm", "prefill.attention", "prefill.o_gemm",
   "prefill.gate_up_geglu_gemm", "prefill.down_gemm",
-  "denoise.time_mlp_modulation_gemv", "denoise.action_in", "denoise.ada_rmsnorm",
+  "denoise.time_mlp_modulation_gemm", "denoise.action_in", "denoise.ada_rmsnorm",
   "denoise.qkv_rope_gemm", "denoise.attention", "denoise.o_gemm", "denoise.gate_up_geglu_gemm",
   "denoise.down_gemm", "denoise.action_out_euler"};
 
@@ -186,14 +192,47 @@ struct Prof {
       cudaEventCreate(&a);
       cudaEventCreate(&b);
     }
-    cudaEventRecord(a, st);
+    cudaEventRecordWithFlags(a, st, cudaEventRecordExternal);  // a graph node under capture
     c->prof.push_back({fam, a, b});
     idx = (int)c->prof.size() - 1;
   }
   ~Prof() {
-    if (idx >= 0) cudaEventRecord(c->prof[idx].b, st);
+    if (idx >= 0) cudaEventRecordWithFlags(c->prof[idx].b, st, cudaEventRecordExternal);
   }
 };
+
+// Launch through cudaLaunchKernelEx: programmatic dependent launch (kernels start their
+// independent prologue while the previous kernel drains) and an optional cluster.
+template <typename... KArgs, typename... Args>
+int launch(pi0_ctx* ctx, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+           cudaStream_t st, dim3 cluster, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[2];
+  int n = 0;
+  if (ctx->pdl) {
+    at[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  if (cluster.x * cluster.y * cluster.z > 1) {
+    at[n].id = cudaLaunchAttributeClusterDimension;
+    at[n].val.clusterDim.x = cluster.x;
+    at[n].val.clusterDim.y = cluster.y;
+    at[n].val.clusterDim.z = cluster.z;
+    ++n;
+  }
+  cfg.attrs = at;
+  cfg.numAttrs = n;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, args...);
+  if (e != cudaSuccess)
+    return fail(ctx, PI0_ERR_CUDA, std::string("cudaLaunchKernelEx: ") + cudaGetErrorString(e));
+  ctx->launches += 1;
+  return 0;
+}
 
 // ---- parameter table (reference export order; see mlc_vla/model/pi0/pi0_model.py) ----------
 void build_table(pi0_ctx* c) {
@@ -265,7 +304,9 @@ int validate(const pi0_config& g, std::string& why) {
   if (g.prefix_len < 1 || g.action_horizon < 1 || g.action_dim < 1 || g.num_denoise_steps < 1)
     return bad("prefix_len, action_horizon, action_dim and num_denoise_steps must be >= 1");
   if (g.max_batch < 1) return bad("max_batch must be >= 1");
-  if (g.ae_width > 4096) return bad("action-expert width above 4096 is not supported");
+  if (g.ae_width > 4096 || g.vlm_width > 4096)
+    return bad("expert widths above 4096 are not supported");
+  if (g.action_dim > 4096) return bad("action_dim above 4096 is not supported");
   return 0;
 }
 
@@ -318,11 +359,74 @@ int gemm_tc_launch(pi0_ctx* ctx, const T* A, int lda, const T* W, int ldw, int M
   const int tiles = ((M + tc::BM - 1) / tc::BM) * ((N + BN - 1) / BN);
   const int grid = std::min(tiles, ctx->num_sms);
   Prof pr(ctx, fam, st);
-  tc::gemm_tc_kernel<T, BN, ST, Epi><<<grid, 192, tc::Smem<BN, ST>::BYTES, st>>>(ta, tb, M, N, K, epi,
-                                                                             ctx->dev_err);
-  ctx->launches += 1;
-  CKL();
-  return 0;
+  return launch(ctx, tc::gemm_tc_kernel<T, BN, ST, Epi>, dim3(grid), dim3(192),
+                tc::Smem<BN, ST>::BYTES, st, dim3(1, 1, 1), ta, tb, M, N, K, epi, ctx->dev_err);
+}
+
+template <typename T>
+int rmsnorm(pi0_ctx* ctx, const T* x, T* out, int rows, int W, const T* w, const T* mod,
+            int rows_per_mod, int mod_stride, cudaStream_t st, int fam);
+template <typename T, class Epi>
+int gemm(pi0_ctx* ctx, const T* A, int lda, const T* W, int ldw, int M, int N, int K,
+         const Epi& epi, cudaStream_t st, int fam, int engine = 0);
+
+// Weight-streaming path for M ≤ 128 activation rows (see gemm_skinny.cuh). Cluster size C (the
+// K split) is the smallest power of two that keeps ≤ KBPC_MAX k-blocks per CTA and gives at
+// least 128 CTAs.
+int skinny_split(int N, int K) {
+  const int nkb = (K + 63) / 64, tiles = (N + 127) / 128;
+  int C = 1;
+  while (C < 16 && C < nkb &&
+         ((nkb + C - 1) / C > sk::KBPC_MAX || tiles * C < 128))
+    C *= 2;
+  return C;
+}
+
+struct SkOpt {
+  const void* wpack = nullptr;  // packed weights (pack_sw128 layout), or null: tensor map on W
+  const void* mod = nullptr;    // NORM: modulation row (scale | shift)
+};
+
+template <typename T, int NA, bool NORM, bool SSQ, class Epi>
+int skinny_launch(pi0_ctx* ctx, const T* X, int ldx, const T* W, int ldw, int M, int N, int K,
+                  const Epi& epi, cudaStream_t st, int fam, SkOpt o) {
+  const int nkb = (K + 63) / 64, tiles = (N + 127) / 128;
+  const int C = skinny_split(N, K);
+  const int kbpc = (nkb + C - 1) / C;
+  if (kbpc > sk::KBPC_MAX) return fail(ctx, PI0_ERR_UNSUPPORTED, "K too large for the weight-streaming GEMM");
+  if (NORM && (K % 8 || K > 4096 || ldx != K))
+    return fail(ctx, PI0_ERR_UNSUPPORTED, "norm-fused GEMM needs K % 8 == 0, K <= 4096, dense rows");
+  if (SSQ && tiles != ctx->ssq_parts)
+    return fail(ctx, PI0_ERR_INVALID, "row-sum partials: tile count differs from ssq_parts");
+  CUtensorMap tw, tx;
+  const bool bf = Tr<T>::kBf16;
+  TRY(make_tmap(ctx, &tw, W, N, K, ldw, tc::BM, bf));
+  TRY(make_tmap(ctx, &tx, X, M, K, ldx, NA, bf));
+  sk::SkArgs a{M, N, K, kbpc, C, ctx->dev_err, o.wpack, X, o.mod, ctx->cfg.rms_norm_eps,
+               ctx->ssq, ctx->ssq, ctx->ssq_parts};
+  Prof pr(ctx, fam, st);
+  return launch(ctx, sk::skinny_kernel<T, NA, NORM, SSQ, Epi>, dim3(tiles * C), dim3(128),
+                sk::SkSmem<NA>::BYTES, st, dim3(C, 1, 1), tw, tx, a, epi);
+}
+
+// Denoise-path projection: the weight-streaming kernel for M ≤ 128 (packed weights `Wp`),
+// the tensor-core tile kernel otherwise (row-major `W`). NORM: the input is adaRMSNorm(A; mod)
+// (fused for M ≤ 128, a separate norm kernel into `scratch` otherwise). SSQ: the epilogue also
+// emits the row Σx² partials of its output stream.
+template <typename T, bool NORM, bool SSQ, class Epi>
+int gemm_w(pi0_ctx* ctx, const T* A, int lda, const T* W, const T* Wp, int M, int N, int K,
+           const Epi& epi, cudaStream_t st, int fam, const T* mod = nullptr,
+           T* scratch = nullptr) {
+  SkOpt o;
+  o.wpack = Wp;
+  o.mod = mod;
+  if (M <= 64) return skinny_launch<T, 64, NORM, SSQ>(ctx, A, lda, W, K, M, N, K, epi, st, fam, o);
+  if (M <= 128) return skinny_launch<T, 128, NORM, SSQ>(ctx, A, lda, W, K, M, N, K, epi, st, fam, o);
+  if (NORM) {
+    TRY(rmsnorm<T>(ctx, A, scratch, M, K, nullptr, mod, M, 0, st, F_DEN_NORM));
+    return gemm<T>(ctx, scratch, K, W, K, M, N, K, epi, st, fam);
+  }
+  return gemm<T>(ctx, A, lda, W, K, M, N, K, epi, st, fam);
 }
 
 // Waves-aware tile width for the tensor-core GEMM: the widest of 256 / 160 / 128 whose last
@@ -362,15 +466,16 @@ int gemm_launch_cfg(pi0_ctx* ctx, const T* A, int lda, const T* W, int ldw, int 
     if ((size_t)grid.x * grid.y > (1u << 16)) return fail(ctx, PI0_ERR_INVALID, "too many tiles");
   }
   Prof pr(ctx, fam, st);
-  kern<<<grid, C::NT, C::SMEM, st>>>(g, epi);
-  ctx->launches += 1;
-  CKL();
-  return 0;
+  return launch(ctx, kern, grid, dim3(C::NT), C::SMEM, st, dim3(1, 1, 1), g, epi);
 }
 
 template <typename T, class Epi>
 int gemm(pi0_ctx* ctx, const T* A, int lda, const T* W, int ldw, int M, int N, int K,
-         const Epi& epi, cudaStream_t st, int fam, int engine = 0) {
+         const Epi& epi, cudaStream_t st, int fam, int engine) {
+  if ((engine == 0 && M <= 128 && ctx->use_tc) || engine == 3) {
+    if (M <= 64) return skinny_launch<T, 64, false, false>(ctx, A, lda, W, ldw, M, N, K, epi, st, fam, SkOpt{});
+    return skinny_launch<T, 128, false, false>(ctx, A, lda, W, ldw, M, N, K, epi, st, fam, SkOpt{});
+  }
   if ((engine == 0 && M >= 128 && ctx->use_tc) || engine == 1) {
     switch (pick_bn(M, N, ctx->num_sms)) {
       case 256: return gemm_tc_launch<T, 256, 4>(ctx, A, lda, W, ldw, M, N, K, epi, st, fam);
@@ -388,21 +493,22 @@ int gemm(pi0_ctx* ctx, const T* A, int lda, const T* W, int ldw, int M, int N, i
 }
 
 // ---- attention launch ----------------------------------------------------------------------
-// Key splits: enough CTAs for two waves over the SMs; keys_per_split is a multiple of ATT_BK.
-int attn_kps(int rows, int batch, int KV, int ltot, int num_sms, bool allow_split) {
+// Key splits (a power of two ≤ 16, so the splits of a row tile form one cluster): grow while
+// the grid stays within two waves over the SMs and every split keeps at least one key tile.
+int attn_splits(int rows, int batch, int KV, int ltot, int num_sms, bool allow_split) {
+  if (!allow_split) return 1;
   const int row_tiles = (rows + ATT_BQ - 1) / ATT_BQ;
+  const int ctas = row_tiles * batch * KV;
   int splits = 1;
-  if (allow_split) {
-    int ctas = row_tiles * batch * KV;
-    splits = std::max(1, (2 * num_sms + ctas - 1) / ctas);
-    splits = std::min(splits, (ltot + ATT_BK - 1) / ATT_BK);
-  }
+  while (splits < 16 && ctas * splits * 2 <= 2 * num_sms &&
+         (ltot + splits * 2 * ATT_BK - 1) / (splits * 2 * ATT_BK) >= 1 &&
+         splits * 2 * ATT_BK <= ltot + ATT_BK)
+    splits *= 2;
+  return splits;
+}
+int attn_kps(int ltot, int splits) {
   int kps = (ltot + splits - 1) / splits;
   return (kps + ATT_BK - 1) / ATT_BK * ATT_BK;
-}
-int attn_splits(int rows, int batch, int KV, int ltot, int num_sms, bool allow_split) {
-  int kps = attn_kps(rows, batch, KV, ltot, num_sms, allow_split);
-  return (ltot + kps - 1) / kps;
 }
 
 template <typename T, int HD>
@@ -412,21 +518,11 @@ int attn_launch_hd(pi0_ctx* ctx, AttnArgs<T> a, int batch, bool allow_split, cud
   const int G = a.H / a.KV, rows = a.Tq * G;
   const int row_tiles = (rows + ATT_BQ - 1) / ATT_BQ;
   const int ltot = a.LA + a.LB;
-  const int kps = attn_kps(rows, batch, a.KV, ltot, ctx->num_sms, allow_split);
-  const int splits = (ltot + kps - 1) / kps;
-  a.keys_per_split = kps;
-  auto kern = attn_kernel<T, HD>;
+  const int splits = attn_splits(rows, batch, a.KV, ltot, ctx->num_sms, allow_split);
+  a.keys_per_split = attn_kps(ltot, splits);
   dim3 grid(row_tiles, splits, batch * a.KV);
-  kern<<<grid, 128, AttnSmem<HD>::BYTES, st>>>(a);
-  ctx->launches += 1;
-  CKL();
-  if (splits > 1) {
-    dim3 g2(rows, batch * a.KV);
-    attn_combine_kernel<T><<<g2, std::max(32, std::min(128, HD / 2)), 0, st>>>(a, HD, splits);
-    ctx->launches += 1;
-    CKL();
-  }
-  return 0;
+  return launch(ctx, attn_kernel<T, HD>, grid, dim3(128), AttnSmem<HD>::BYTES, st,
+                dim3(1, splits, 1), a);
 }
 
 template <typename T>
@@ -447,28 +543,9 @@ template <typename T>
 int rmsnorm(pi0_ctx* ctx, const T* x, T* out, int rows, int W, const T* w, const T* mod,
             int rows_per_mod, int mod_stride, cudaStream_t st, int fam) {
   Prof pr(ctx, fam, st);
-  ctx->launches += 1;
   int blocks = (rows + 7) / 8;
-  rmsnorm_kernel<T><<<blocks, 256, 0, st>>>(x, out, rows, W, ctx->cfg.rms_norm_eps, w, mod,
-                                            rows_per_mod, mod_stride);
-  CKL();
-  return 0;
-}
-
-template <typename T>
-int gemv(pi0_ctx* ctx, const T* x, int M, int K, const T* W, const T* b, int N, T* y, int ldy,
-         int silu, cudaStream_t st) {
-  Prof pr(ctx, F_DEN_TIME_MODS, st);
-  for (int m0 = 0; m0 < M; m0 += GEMV_MMAX) {
-    ctx->launches += 1;
-    int mm = std::min(GEMV_MMAX, M - m0);
-    size_t smem = (size_t)mm * K * sizeof(float);
-    int blocks = std::min((N + 7) / 8, ctx->num_sms * 8);
-    gemv_kernel<T><<<blocks, 256, smem, st>>>(x + (size_t)m0 * K, mm, K, W, b, N,
-                                              y + (size_t)m0 * ldy, ldy, silu);
-    CKL();
-  }
-  return 0;
+  return launch(ctx, rmsnorm_kernel<T>, dim3(blocks), dim3(256), 0, st, dim3(1, 1, 1), x, out, rows, W,
+                ctx->cfg.rms_norm_eps, w, mod, rows_per_mod, mod_stride);
 }
 
 // time conditions and all 2·L+1 modulations for `nsteps` time embeddings [nsteps, W1]
@@ -479,10 +556,24 @@ int time_and_mods(pi0_ctx* ctx, const T* te, int nsteps, cudaStream_t st) {
   const int nmod = (2 * g.depth + 1) * 3 * W1;
   T* t1 = (T*)ctx->t1;
   T* cond = (T*)ctx->cond;
-  TRY(gemv<T>(ctx, te, nsteps, W1, (const T*)ctx->tin_w, (const T*)ctx->tin_b, W1, t1, W1, 1, st));
-  TRY(gemv<T>(ctx, t1, nsteps, W1, (const T*)ctx->tout_w, (const T*)ctx->tout_b, W1, cond, W1, 1, st));
-  TRY(gemv<T>(ctx, cond, nsteps, W1, (const T*)ctx->mod_w, (const T*)ctx->mod_b, nmod,
-              (T*)ctx->mods, nmod, 0, st));
+  // three weight-streaming GEMMs with M = nsteps: time_mlp_in + SiLU, time_mlp_out + SiLU, and
+  // every adaRMS modulation of the step(s) at once
+  for (int m0 = 0; m0 < nsteps; m0 += 64) {
+    const int mm = std::min(64, nsteps - m0);
+    TRY((gemm_w<T, false, false>(ctx, te + (size_t)m0 * W1, W1, (const T*)ctx->tin_w,
+                                 (const T*)ctx->tin_p, mm, W1, W1,
+                                 EpiStore<T>{t1 + (size_t)m0 * W1, W1, (const T*)ctx->tin_b, 1}, st,
+                                 F_DEN_TIME_MODS)));
+    TRY((gemm_w<T, false, false>(ctx, t1 + (size_t)m0 * W1, W1, (const T*)ctx->tout_w,
+                                 (const T*)ctx->tout_p, mm, W1, W1,
+                                 EpiStore<T>{cond + (size_t)m0 * W1, W1, (const T*)ctx->tout_b, 1},
+                                 st, F_DEN_TIME_MODS)));
+    TRY((gemm_w<T, false, false>(ctx, cond + (size_t)m0 * W1, W1, (const T*)ctx->mod_w,
+                                 (const T*)ctx->mod_w_p, mm, nmod, W1,
+                                 EpiStore<T>{(T*)ctx->mods + (size_t)m0 * nmod, nmod,
+                                             (const T*)ctx->mod_b, 0},
+                                 st, F_DEN_TIME_MODS)));
+  }
   return 0;
 }
 
@@ -528,8 +619,6 @@ int run_prefill(pi0_ctx* ctx, int B, const T* prefix, const float* mask, float* 
     a.H = H;
     a.KV = KV;
     a.out = attn;
-    a.part_o = ctx->part_o;
-    a.part_ml = ctx->part_ml;
     TRY(attn_launch<T>(ctx, a, B, false, st, F_PRE_ATTN));
     TRY(gemm<T>(ctx, attn, hq, (const T*)w.o, hq, M, W0, hq, EpiResid<T>{x, W0}, st, F_PRE_O));
     TRY(rmsnorm<T>(ctx, x, xn, M, W0, (const T*)w.ln_post, nullptr, 1, 0, st, F_PRE_NORM));
@@ -558,25 +647,24 @@ int run_suffix(pi0_ctx* ctx, int B, const float* keys, const T* values, const vo
   T* h = (T*)ctx->hs;
   {
     Prof pr(ctx, F_DEN_ACT_IN, st);
-    ctx->launches += 1;
-    int n = M * W1;
+    const size_t sm = (size_t)D * sizeof(float);
+    float* ssq = M <= 128 ? ctx->ssq : nullptr;
     if (x_is_f32)
-      action_in_kernel<T, true><<<(n + 255) / 256, 256, 0, st>>>(x_in, M, D, (const T*)ctx->ain_w,
-                                                                 (const T*)ctx->ain_b, W1, x);
+      TRY(launch(ctx, action_in_kernel<T, true>, dim3(M), dim3(256), sm, st, dim3(1, 1, 1), x_in, M, D,
+                 (const T*)ctx->ain_w, (const T*)ctx->ain_b, W1, x, ssq, ctx->ssq_parts));
     else
-      action_in_kernel<T, false><<<(n + 255) / 256, 256, 0, st>>>(x_in, M, D, (const T*)ctx->ain_w,
-                                                                  (const T*)ctx->ain_b, W1, x);
-    CKL();
+      TRY(launch(ctx, action_in_kernel<T, false>, dim3(M), dim3(256), sm, st, dim3(1, 1, 1), x_in, M, D,
+                 (const T*)ctx->ain_w, (const T*)ctx->ain_b, W1, x, ssq, ctx->ssq_parts));
   }
   const size_t kv_layer = (size_t)B * KV * P * hd;
   for (int l = 0; l < g.depth; ++l) {
     const LayerW& w = ctx->suf[l];
     const T* m_in = mods + (size_t)(2 * l) * mstride;
     const T* m_post = mods + (size_t)(2 * l + 1) * mstride;
-    TRY(rmsnorm<T>(ctx, x, xn, M, W1, nullptr, m_in, M, 0, st, F_DEN_NORM));
     EpiQkvRope<T> eq{ctx->qs, ctx->ksuf, (T*)ctx->vsuf, scos, ssin, S * (hd / 2), S, H, KV, hd, 0,
                      (float)std::pow((double)hd, -0.5)};
-    TRY(gemm<T>(ctx, xn, W1, (const T*)w.qkv, W1, M, hq + 2 * hkv, W1, eq, st, F_DEN_QKV));
+    TRY((gemm_w<T, true, false>(ctx, x, W1, (const T*)w.qkv, (const T*)w.qkv_p, M, hq + 2 * hkv,
+                                W1, eq, st, F_DEN_QKV, m_in, xn)));
     AttnArgs<T> a{};
     a.q = ctx->qs;
     a.kA = keys + l * kv_layer;
@@ -590,26 +678,22 @@ int run_suffix(pi0_ctx* ctx, int B, const float* keys, const T* values, const vo
     a.H = H;
     a.KV = KV;
     a.out = attn;
-    a.part_o = ctx->part_o;
-    a.part_ml = ctx->part_ml;
+    a.a_is_ready = 1;  // the prefix K/V cache comes from prefill, not from this step
     TRY(attn_launch<T>(ctx, a, B, true, st, F_DEN_ATTN));
-    TRY(gemm<T>(ctx, attn, hq, (const T*)w.o, hq, M, W1, hq,
-                EpiGatedResid<T>{x, W1, m_in + 2 * W1, M, 0}, st, F_DEN_O));
-    TRY(rmsnorm<T>(ctx, x, xn, M, W1, nullptr, m_post, M, 0, st, F_DEN_NORM));
-    TRY(gemm<T>(ctx, xn, W1, (const T*)w.gu, W1, M, 2 * F1, W1, EpiGeglu<T>{h, F1}, st,
-                F_DEN_GU));
-    TRY(gemm<T>(ctx, h, F1, (const T*)w.d, F1, M, W1, F1,
-                EpiGatedResid<T>{x, W1, m_post + 2 * W1, M, 0}, st, F_DEN_DOWN));
+    TRY((gemm_w<T, false, true>(ctx, attn, hq, (const T*)w.o, (const T*)w.o_p, M, W1, hq,
+                                EpiGatedResid<T>{x, W1, m_in + 2 * W1, M, 0}, st, F_DEN_O)));
+    TRY((gemm_w<T, true, false>(ctx, x, W1, (const T*)w.gu, (const T*)w.gu_p, M, 2 * F1, W1,
+                                EpiGeglu<T>{h, F1}, st, F_DEN_GU, m_post, xn)));
+    TRY((gemm_w<T, false, true>(ctx, h, F1, (const T*)w.d, (const T*)w.d_p, M, W1, F1,
+                                EpiGatedResid<T>{x, W1, m_post + 2 * W1, M, 0}, st, F_DEN_DOWN)));
   }
-  TRY(rmsnorm<T>(ctx, x, xn, M, W1, nullptr, mods + (size_t)(2 * g.depth) * mstride, M, 0, st,
-                 F_DEN_NORM));
   {
     Prof pr(ctx, F_DEN_ACT_OUT, st);
-    ctx->launches += 1;
     int warps = M * D;
-    action_out_kernel<T><<<(warps * 32 + 255) / 256, 256, 0, st>>>(
-        xn, M, W1, (const T*)ctx->aout_w, (const T*)ctx->aout_b, D, out, euler, dt);
-    CKL();
+    TRY(launch(ctx, action_out_kernel<T>, dim3((warps * 32 + 255) / 256), dim3(256), 0, st,
+               dim3(1, 1, 1),
+               (const T*)x, M, W1, mods + (size_t)(2 * g.depth) * mstride, ctx->cfg.rms_norm_eps,
+               (const T*)ctx->aout_w, (const T*)ctx->aout_b, D, out, euler, dt));
   }
   return 0;
 }
@@ -655,8 +739,18 @@ int attr_tc(pi0_ctx* ctx) {
                           cudaFuncAttributeMaxDynamicSharedMemorySize, tc::Smem<BN, ST>::BYTES));
   return 0;
 }
+template <typename T, int NA, class Epi, bool SSQ = false>
+int attr_sk(pi0_ctx* ctx) {
+  for (auto k : {sk::skinny_kernel<T, NA, false, SSQ, Epi>, sk::skinny_kernel<T, NA, !SSQ, SSQ, Epi>}) {
+    CK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, sk::SkSmem<NA>::BYTES));
+    CK(cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+  }
+  return 0;
+}
 template <typename T, class Epi>
 int attr_gemm_both(pi0_ctx* ctx) {
+  TRY((attr_sk<T, 64, Epi>(ctx)));
+  TRY((attr_sk<T, 128, Epi>(ctx)));
   TRY((attr_gemm<T, 128, 128, 64, 32, 4, Epi>(ctx)));
   TRY((attr_gemm<T, 64, 64, 32, 32, 4, Epi>(ctx)));
   TRY((attr_tc<T, 256, 4, Epi>(ctx)));
@@ -668,6 +762,7 @@ template <typename T, int HD>
 int attr_attn(pi0_ctx* ctx) {
   CK(cudaFuncSetAttribute(attn_kernel<T, HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                           AttnSmem<HD>::BYTES));
+  CK(cudaFuncSetAttribute(attn_kernel<T, HD>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
   return 0;
 }
 template <typename T>
@@ -675,6 +770,8 @@ int setup_attrs(pi0_ctx* ctx) {
   TRY(attr_gemm_both<T, EpiQkvRope<T>>(ctx));
   TRY(attr_gemm_both<T, EpiResid<T>>(ctx));
   TRY(attr_gemm_both<T, EpiGatedResid<T>>(ctx));
+  TRY((attr_sk<T, 64, EpiGatedResid<T>, true>(ctx)));
+  TRY((attr_sk<T, 128, EpiGatedResid<T>, true>(ctx)));
   TRY(attr_gemm_both<T, EpiGeglu<T>>(ctx));
   TRY(attr_gemm_both<T, EpiStore<T>>(ctx));
   switch (ctx->cfg.head_dim) {
@@ -684,8 +781,6 @@ int setup_attrs(pi0_ctx* ctx) {
     case 128: TRY((attr_attn<T, 128>(ctx))); break;
     case 256: TRY((attr_attn<T, 256>(ctx))); break;
   }
-  int gemv_smem = GEMV_MMAX * std::max(ctx->cfg.ae_width, 1) * 4;
-  CK(cudaFuncSetAttribute(gemv_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, gemv_smem));
   return 0;
 }
 
@@ -745,6 +840,12 @@ int alloc_all(pi0_ctx* ctx) {
              pad(W1 * F1);
   arena += pad(nmodw * W1) + pad(nmodw) + pad(W1 * D) + pad(W1) + pad(D * W1) + pad(D) +
            2 * (pad(W1 * W1) + pad(W1));
+  // packed copies of the weight-streaming matrices (action expert, modulations, time MLP)
+  auto packed = [&](size_t n, size_t k) {
+    return ((n + 127) / 128) * ((k + 63) / 64) * (size_t)sk::W_BLOCK;
+  };
+  arena += L * (packed(hq + 2 * hkv, W1) + packed(W1, hq) + packed(2 * F1, W1) + packed(W1, F1)) +
+           packed(nmodw, W1) + 2 * packed(W1, W1);
   ctx->arena_bytes = arena;
   TRY(dev_alloc(ctx, &ctx->arena, ctx->arena_bytes));
   char* p = (char*)ctx->arena;
@@ -780,6 +881,23 @@ int alloc_all(pi0_ctx* ctx) {
   ctx->tin_b = take(W1);
   ctx->tout_w = take(W1 * W1);
   ctx->tout_b = take(W1);
+  auto take_bytes = [&](size_t bytes) {
+    void* r = p;
+    p += bytes;
+    return r;
+  };
+  for (int l = 0; l < L; ++l) {
+    LayerW& w = ctx->suf[l];
+    w.qkv_p = take_bytes(packed(hq + 2 * hkv, W1));
+    w.o_p = take_bytes(packed(W1, hq));
+    w.gu_p = take_bytes(packed(2 * F1, W1));
+    w.d_p = take_bytes(packed(W1, F1));
+  }
+  ctx->mod_w_p = take_bytes(packed(nmodw, W1));
+  ctx->tin_p = take_bytes(packed(W1, W1));
+  ctx->tout_p = take_bytes(packed(W1, W1));
+  if ((size_t)(p - (char*)ctx->arena) > ctx->arena_bytes)
+    return fail(ctx, PI0_ERR_INVALID, "internal: weight arena overflow");
 
   // permutations and the prefix RoPE table (float64 -> fp32, gemma_dual.py:24-44)
   TRY(upload_ints(ctx, &ctx->perm_q, rope_perm(H, hd)));
@@ -818,13 +936,6 @@ int alloc_all(pi0_ctx* ctx) {
   TRY(dev_alloc(ctx, &ctx->t1, (size_t)N * W1 * e));
   TRY(dev_alloc(ctx, &ctx->cond, (size_t)N * W1 * e));
   TRY(dev_alloc(ctx, &ctx->mods, (size_t)N * nmodw * e));
-  // attention split partials of the denoise attention: max over batch sizes of B·splits(B)
-  const int rows = (int)S * (H / KV);
-  size_t bs_max = 1;
-  for (int b = 1; b <= (int)B; ++b)
-    bs_max = std::max(bs_max, (size_t)b * attn_splits(rows, b, KV, (int)(P + S), ctx->num_sms, true));
-  TRY(dev_alloc(ctx, (void**)&ctx->part_o, bs_max * KV * rows * hd * 4));
-  TRY(dev_alloc(ctx, (void**)&ctx->part_ml, bs_max * KV * rows * 2 * 4));
   // split-K partials (GEMMs with M < 256 only): splits·M·N ≤ (2·SMs/tiles + 1)·M·N
   //   ≤ 2·SMs·64·64 + 256·maxN
   size_t maxN = std::max(std::max(hq + 2 * hkv, 2 * F1), std::max(std::max(W1, W0), 2 * F0));
@@ -833,6 +944,8 @@ int alloc_all(pi0_ctx* ctx) {
   TRY(dev_alloc(ctx, (void**)&ctx->tickets, (1 << 16) * 4));
   CK(cudaMemset(ctx->tickets, 0, (1 << 16) * 4));
   TRY(dev_alloc(ctx, (void**)&ctx->dev_err, 16));
+  ctx->ssq_parts = (int)((W1 + 127) / 128);
+  TRY(dev_alloc(ctx, (void**)&ctx->ssq, MS * ctx->ssq_parts * 4));
   CK(cudaMemset(ctx->dev_err, 0, 16));
   return 0;
 }
@@ -885,10 +998,57 @@ int set_params_impl(pi0_ctx* ctx, const void* const* params, cudaStream_t st) {
       case R_TOUT_B: TRY(copy(ctx, ctx->tout_b, src, W1 * e, st)); break;
     }
   }
+  // pack the weight-streaming matrices (from the repacked row-major copies above)
+  auto pack = [&](void* dst, const void* src, size_t n, size_t k) -> int {
+    const int nkb = (int)((k + 63) / 64);
+    const size_t chunks = ((n + 127) / 128) * nkb * 128 * 8;
+    sk::pack_sw128_kernel<<<(unsigned)((chunks + 255) / 256), 256, 0, st>>>(
+        (uint16_t*)dst, (const uint16_t*)src, (int)n, (int)k, nkb, chunks);
+    CKL();
+    return 0;
+  };
+  for (int l = 0; l < g.depth; ++l) {
+    const LayerW& w = ctx->suf[l];
+    TRY(pack(w.qkv_p, w.qkv, hq + 2 * hkv, W[1]));
+    TRY(pack(w.o_p, w.o, W[1], hq));
+    TRY(pack(w.gu_p, w.gu, 2 * F[1], W[1]));
+    TRY(pack(w.d_p, w.d, W[1], F[1]));
+  }
+  TRY(pack(ctx->mod_w_p, ctx->mod_w, (size_t)(2 * g.depth + 1) * 3 * W1, W1));
+  TRY(pack(ctx->tin_p, ctx->tin_w, W1, W1));
+  TRY(pack(ctx->tout_p, ctx->tout_w, W1, W1));
   return 0;
 }
 
 bool is_bf16(const pi0_ctx* c) { return c->cfg.dtype == PI0_BF16; }
+
+// Profiling mode: capture `body` (kernel launches and the event records that bracket them) into
+// a one-shot graph and replay it on `stream`, so the recorded intervals are device time without
+// host launch gaps.
+template <class F>
+int run_profiled(pi0_ctx* ctx, cudaStream_t stream, F body) {
+  cudaStream_t cs = ctx->cap_stream;
+  CK(cudaStreamSynchronize(stream));
+  CK(cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal));
+  int r = body(cs);
+  cudaGraph_t graph = nullptr;
+  cudaError_t ce = cudaStreamEndCapture(cs, &graph);
+  if (r) {
+    if (graph) cudaGraphDestroy(graph);
+    return r;
+  }
+  if (ce != cudaSuccess) return fail(ctx, PI0_ERR_CUDA, std::string("capture: ") + cudaGetErrorString(ce));
+  cudaGraphExec_t exec = nullptr;
+  ce = cudaGraphInstantiate(&exec, graph, 0);
+  cudaGraphDestroy(graph);
+  if (ce != cudaSuccess) return fail(ctx, PI0_ERR_CUDA, std::string("instantiate: ") + cudaGetErrorString(ce));
+  ce = cudaGraphLaunch(exec, stream);
+  cudaError_t ce2 = cudaStreamSynchronize(stream);
+  cudaGraphExecDestroy(exec);
+  if (ce != cudaSuccess || ce2 != cudaSuccess)
+    return fail(ctx, PI0_ERR_CUDA, std::string("profiled replay: ") + cudaGetErrorString(ce != cudaSuccess ? ce : ce2));
+  return 0;
+}
 
 int check_ready(pi0_ctx* ctx, int batch) {
   if (!ctx) return PI0_ERR_INVALID;
@@ -987,11 +1147,15 @@ int pi0_prefill(pi0_ctx* ctx, int batch, const void* prefix_embs, const float* p
   TRY(check_ready(ctx, batch));
   if (!prefix_embs || !prefix_mask || !keys || !values)
     return fail(ctx, PI0_ERR_INVALID, "null tensor argument");
-  if (is_bf16(ctx))
-    return run_prefill<__nv_bfloat16>(ctx, batch, (const __nv_bfloat16*)prefix_embs, prefix_mask,
-                                      keys, (__nv_bfloat16*)values, stream);
-  return run_prefill<__half>(ctx, batch, (const __half*)prefix_embs, prefix_mask, keys,
-                             (__half*)values, stream);
+  auto body = [&](cudaStream_t st) {
+    if (is_bf16(ctx))
+      return run_prefill<__nv_bfloat16>(ctx, batch, (const __nv_bfloat16*)prefix_embs, prefix_mask,
+                                        keys, (__nv_bfloat16*)values, st);
+    return run_prefill<__half>(ctx, batch, (const __half*)prefix_embs, prefix_mask, keys,
+                               (__half*)values, st);
+  };
+  if (ctx->prof_on) return run_profiled(ctx, stream, body);
+  return body(stream);
 }
 
 int pi0_denoise_step_kv(pi0_ctx* ctx, int batch, const float* keys, const void* values,
@@ -1026,7 +1190,7 @@ int pi0_denoise_loop_kv(pi0_ctx* ctx, int batch, const float* keys, const void* 
                                        (const __half*)time_embs, suffix_cos, suffix_sin,
                                        prefix_mask, x_out, cs);
   };
-  if (ctx->prof_on) return body(stream);  // eager, so every launch can be timed
+  if (ctx->prof_on) return run_profiled(ctx, stream, body);
   GraphKey key{batch, {keys, values, x0, time_embs, suffix_cos, suffix_sin, prefix_mask, x_out,
                        nullptr}};
   auto it = ctx->graphs.find(key);

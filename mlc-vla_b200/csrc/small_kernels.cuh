@@ -1,6 +1,6 @@
-// Row-wise and skinny kernels of the M1 path: RMSNorm (plain and adaRMS), the GEMV that
-// streams the time-MLP and adaRMS-modulation weights, the action in/out projections (K or N
-// equal to action_dim) with the Euler update fused, weight repacking and group quantisation.
+// Row-wise kernels of the M1 path: RMSNorm (plain and adaRMS), the action in/out projections
+// (K or N equal to action_dim) with the Euler update fused, weight repacking and group
+// quantisation.
 #pragma once
 
 #include "common.cuh"
@@ -10,135 +10,168 @@ namespace pi0 {
 // ---- RMSNorm (gemma_dual.py:75-89) -------------------------------------------------------
 // normed = x / sqrt(Σx²/W + eps) in fp32; plain: ·(1 + w); ada: ·(1 + scale) + shift, where
 // (scale, shift) = mod[0:W], mod[W:2W] of the modulation row of the request's group
-// (mod + (row / rows_per_mod) · mod_stride). One warp per row; output in the model dtype.
+// (mod + (row / rows_per_mod) · mod_stride). One warp per row; every lane issues all of its
+// 16-byte loads before using any (W ≤ 32·8·RMS_CHUNKS). Output in the model dtype.
+constexpr int RMS_CHUNKS = 16;
+
 template <typename T>
 __global__ void rmsnorm_kernel(const T* __restrict__ x, T* __restrict__ out, int rows, int W,
                                float eps, const T* __restrict__ w, const T* __restrict__ mod,
                                int rows_per_mod, int mod_stride) {
+  pdl_wait();
+  pdl_trigger();
   int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   int lane = threadIdx.x & 31;
   if (row >= rows) return;
-  const T* xr = x + (size_t)row * W;
+  const int nch = W / 8;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)row * W);
+  uint4 xv[RMS_CHUNKS];
+#pragma unroll
+  for (int c = 0; c < RMS_CHUNKS; ++c)
+    if (c * 32 + lane < nch) xv[c] = __ldg(xr + c * 32 + lane);
   float ss = 0.f;
-  for (int i = lane * 2; i < W; i += 64) {
-    float a = Tr<T>::f(xr[i]), b = Tr<T>::f(xr[i + 1]);
-    ss += a * a + b * b;
-  }
+#pragma unroll
+  for (int c = 0; c < RMS_CHUNKS; ++c)
+    if (c * 32 + lane < nch) {
+      const T* e = reinterpret_cast<const T*>(&xv[c]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float f = Tr<T>::f(e[j]);
+        ss += f * f;
+      }
+    }
   ss = warp_sum(ss);
   const float denom = sqrtf(__fadd_rn(__fdiv_rn(ss, (float)W), eps));
   const T* m = mod ? mod + (size_t)(row / rows_per_mod) * mod_stride : nullptr;
-  T* o = out + (size_t)row * W;
-  for (int i = lane * 2; i < W; i += 64) {
-    float r[2];
+  uint4* o = reinterpret_cast<uint4*>(out + (size_t)row * W);
 #pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      float n = __fdiv_rn(Tr<T>::f(xr[i + e]), denom);
-      if (m) {
-        r[e] = __fadd_rn(__fmul_rn(n, __fadd_rn(1.f, Tr<T>::f(m[i + e]))), Tr<T>::f(m[W + i + e]));
-      } else {
-        r[e] = __fmul_rn(n, __fadd_rn(1.f, Tr<T>::f(w[i + e])));
-      }
+  for (int c = 0; c < RMS_CHUNKS; ++c) {
+    const int ch = c * 32 + lane;
+    if (ch >= nch) continue;
+    const T* e = reinterpret_cast<const T*>(&xv[c]);
+    uint4 a, b;
+    if (m) {
+      a = __ldg(reinterpret_cast<const uint4*>(m) + ch);          // scale
+      b = __ldg(reinterpret_cast<const uint4*>(m + W) + ch);      // shift
+    } else {
+      a = __ldg(reinterpret_cast<const uint4*>(w) + ch);
     }
-    *reinterpret_cast<uint32_t*>(o + i) = Tr<T>::pack(r[0], r[1]);
-  }
-}
-
-// ---- GEMV for M ≤ GEMV_MMAX rows (time MLP, adaRMS modulations) --------------------------
-// y[m, n] = act(round(round(Σ_k x[m,k]·W[n,k]) + b[n])), act ∈ {identity, silu→round}.
-// One warp per weight row; 16-byte coalesced weight loads, four in flight per lane; x staged
-// in shared memory as fp32. Each output's reduction order depends only on K, not on M, so the
-// hoisted all-steps modulation (M = N steps) equals N single-step launches bit for bit.
-constexpr int GEMV_MMAX = 16;
-
-template <typename T>
-__global__ void __launch_bounds__(256) gemv_kernel(const T* __restrict__ x, int M, int K,
-                                                   const T* __restrict__ W,
-                                                   const T* __restrict__ bias, int N,
-                                                   T* __restrict__ y, int ldy, int act_silu) {
-  extern __shared__ float sx[];  // [M][K]
-  for (int i = threadIdx.x; i < M * K; i += blockDim.x) sx[i] = Tr<T>::f(x[i]);
-  __syncthreads();
-  const int lane = threadIdx.x & 31;
-  const int warps = blockDim.x / 32;
-  for (int n = blockIdx.x * warps + threadIdx.x / 32; n < N; n += gridDim.x * warps) {
-    const T* wr = W + (size_t)n * K;
-    float acc[GEMV_MMAX];
+    const T* sa = reinterpret_cast<const T*>(&a);
+    const T* sb = reinterpret_cast<const T*>(&b);
+    uint32_t res[4];
 #pragma unroll
-    for (int m = 0; m < GEMV_MMAX; ++m) acc[m] = 0.f;
-    for (int k0 = lane * 8; k0 < K; k0 += 32 * 8 * 4) {
-      uint4 wv[4];
+    for (int j = 0; j < 4; ++j) {
+      float r2[2];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        int k = k0 + u * 256;
-        wv[u] = k < K ? __ldg(reinterpret_cast<const uint4*>(wr + k)) : make_uint4(0, 0, 0, 0);
+      for (int h = 0; h < 2; ++h) {
+        const int q = 2 * j + h;
+        float n = __fdiv_rn(Tr<T>::f(e[q]), denom);
+        r2[h] = m ? __fadd_rn(__fmul_rn(n, __fadd_rn(1.f, Tr<T>::f(sa[q]))), Tr<T>::f(sb[q]))
+                  : __fmul_rn(n, __fadd_rn(1.f, Tr<T>::f(sa[q])));
       }
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        int k = k0 + u * 256;
-        if (k >= K) break;
-        const T* wh = reinterpret_cast<const T*>(&wv[u]);
-        float wf[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) wf[e] = Tr<T>::f(wh[e]);
-#pragma unroll
-        for (int m = 0; m < GEMV_MMAX; ++m) {
-          if (m < M) {
-            const float* xs = sx + m * K + k;
-#pragma unroll
-            for (int e = 0; e < 8; ++e) acc[m] = fmaf(wf[e], xs[e], acc[m]);
-          }
-        }
-      }
+      res[j] = Tr<T>::pack(r2[0], r2[1]);
     }
-#pragma unroll
-    for (int m = 0; m < GEMV_MMAX; ++m) {
-      if (m < M) {
-        float v = warp_sum(acc[m]);
-        if (lane == 0) {
-          float r = Tr<T>::r(v);
-          if (bias) r = Tr<T>::r(r + Tr<T>::f(bias[n]));
-          if (act_silu) r = Tr<T>::r(silu_f(r));
-          y[(size_t)m * ldy + n] = Tr<T>::t(r);
-        }
-      }
-    }
+    o[ch] = make_uint4(res[0], res[1], res[2], res[3]);
   }
 }
 
 // ---- action_in_proj (pi0_model.py:154,187): emb = round(round(x·Wᵀ) + b), K = action_dim ----
 // x is the model-dtype x_t (XF32 = false) or the fp32 Euler state cast to the model dtype.
+// One block per activation row: the row is staged in shared memory, each thread produces
+// Wd / blockDim outputs.
+// Also emits the row's Σ emb² into ssq[r·ssq_parts] (other parts zero) for the first norm-fused
+// GEMM when ssq is not null.
 template <typename T, bool XF32>
 __global__ void action_in_kernel(const void* __restrict__ xin, int rows, int D,
                                  const T* __restrict__ W, const T* __restrict__ b, int Wd,
-                                 T* __restrict__ out) {
-  int idx = blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx >= rows * Wd) return;
-  int r = idx / Wd, n = idx - r * Wd;
-  float acc = 0.f;
-  for (int k = 0; k < D; ++k) {
-    float xv = XF32 ? Tr<T>::r(reinterpret_cast<const float*>(xin)[(size_t)r * D + k])
-                    : Tr<T>::f(reinterpret_cast<const T*>(xin)[(size_t)r * D + k]);
-    acc = fmaf(xv, Tr<T>::f(W[(size_t)n * D + k]), acc);
+                                 T* __restrict__ out, float* __restrict__ ssq, int ssq_parts) {
+  extern __shared__ float sxr[];
+  __shared__ float s_red[32];
+  pdl_wait();
+  pdl_trigger();
+  const int r = blockIdx.x;
+  for (int k = threadIdx.x; k < D; k += blockDim.x)
+    sxr[k] = XF32 ? Tr<T>::r(reinterpret_cast<const float*>(xin)[(size_t)r * D + k])
+                  : Tr<T>::f(reinterpret_cast<const T*>(xin)[(size_t)r * D + k]);
+  __syncthreads();
+  float sq = 0.f;
+  for (int n = threadIdx.x; n < Wd; n += blockDim.x) {
+    const T* wr = W + (size_t)n * D;
+    float acc = 0.f;
+#pragma unroll 8
+    for (int k = 0; k < D; ++k) acc = fmaf(sxr[k], Tr<T>::f(wr[k]), acc);
+    const float y = Tr<T>::r(Tr<T>::r(acc) + Tr<T>::f(b[n]));
+    out[(size_t)r * Wd + n] = Tr<T>::t(y);
+    sq += y * y;
   }
-  float y = Tr<T>::r(Tr<T>::r(acc) + Tr<T>::f(b[n]));
-  out[idx] = Tr<T>::t(y);
+  if (ssq) {
+    sq = warp_sum(sq);
+    if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = sq;
+    __syncthreads();
+    if (threadIdx.x < ssq_parts) {
+      float t = 0.f;
+      if (threadIdx.x == 0)
+        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += s_red[w];
+      ssq[(size_t)r * ssq_parts + threadIdx.x] = t;
+    }
+  }
 }
 
-// ---- action_out_proj (pi0_model.py:162-163,192-193) ---------------------------------------
-// v = float(round(round(h·Wᵀ) + b)); euler = 0: v_out = v; euler = 1: x = x + dt·v (fp32,
-// no fused multiply-add, as numpy and the reference's separate multiply and add).
+// ---- final adaRMSNorm + action_out_proj (gemma_dual.py:432; pi0_model.py:162-163,192-193) --
+// h = round(norm(x; mod)) with the final norm's modulation (scale, shift); v = float(round(
+// round(h·Wᵀ) + b)); euler = 0: v_out = v; euler = 1: x = x + dt·v (fp32, no fused
+// multiply-add, as numpy and the reference's separate multiply and add). One warp per (row, d).
 template <typename T>
 __global__ void action_out_kernel(const T* __restrict__ h, int rows, int Wd,
+                                  const T* __restrict__ mod, float eps,
                                   const T* __restrict__ W, const T* __restrict__ b, int D,
                                   float* __restrict__ out, int euler, float dt) {
+  pdl_wait();
+  pdl_trigger();
   int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (warp >= rows * D) return;
   int r = warp / D, d = warp - r * D;
-  const T* hr = h + (size_t)r * Wd;
-  const T* wr = W + (size_t)d * Wd;
+  const uint4* hr = reinterpret_cast<const uint4*>(h + (size_t)r * Wd);
+  const uint4* wr = reinterpret_cast<const uint4*>(W + (size_t)d * Wd);
+  const int nch = Wd / 8;
+  uint4 hv[RMS_CHUNKS], wv[RMS_CHUNKS];
+#pragma unroll
+  for (int c = 0; c < RMS_CHUNKS; ++c)
+    if (c * 32 + lane < nch) {
+      hv[c] = __ldg(hr + c * 32 + lane);
+      wv[c] = __ldg(wr + c * 32 + lane);
+    }
+  float ss = 0.f;
+#pragma unroll
+  for (int c = 0; c < RMS_CHUNKS; ++c)
+    if (c * 32 + lane < nch) {
+      const T* a = reinterpret_cast<const T*>(&hv[c]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float f = Tr<T>::f(a[j]);
+        ss += f * f;
+      }
+    }
+  ss = warp_sum(ss);
+  const float denom = sqrtf(__fadd_rn(__fdiv_rn(ss, (float)Wd), eps));
   float acc = 0.f;
-  for (int k = lane * 2; k < Wd; k += 64)
-    acc += Tr<T>::f(hr[k]) * Tr<T>::f(wr[k]) + Tr<T>::f(hr[k + 1]) * Tr<T>::f(wr[k + 1]);
+#pragma unroll
+  for (int c = 0; c < RMS_CHUNKS; ++c)
+    if (c * 32 + lane < nch) {
+      const int ch = c * 32 + lane;
+      const uint4 sc = __ldg(reinterpret_cast<const uint4*>(mod) + ch);
+      const uint4 sh = __ldg(reinterpret_cast<const uint4*>(mod + Wd) + ch);
+      const T* a = reinterpret_cast<const T*>(&hv[c]);
+      const T* es = reinterpret_cast<const T*>(&sc);
+      const T* eh = reinterpret_cast<const T*>(&sh);
+      const T* bb = reinterpret_cast<const T*>(&wv[c]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float n = __fdiv_rn(Tr<T>::f(a[j]), denom);
+        const float hn = Tr<T>::r(__fadd_rn(__fmul_rn(n, __fadd_rn(1.f, Tr<T>::f(es[j]))), Tr<T>::f(eh[j])));
+        acc = fmaf(hn, Tr<T>::f(bb[j]), acc);
+      }
+    }
   acc = warp_sum(acc);
   if (lane == 0) {
     float v = Tr<T>::r(Tr<T>::r(acc) + Tr<T>::f(b[d]));

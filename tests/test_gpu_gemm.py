@@ -16,12 +16,18 @@ def rt():
     return Pi0Runtime(config(recipes.MINI), device=0)
 
 
-@pytest.mark.parametrize("engine", [1, 2])
+@pytest.mark.parametrize("engine", [1, 2, 3])
 @pytest.mark.parametrize("m,n,k", [(128, 256, 64), (968, 2560, 2048), (200, 160, 320),
-                                   (50, 1024, 4096), (777, 390, 96), (1000, 32768, 128)])
+                                   (50, 1024, 4096), (777, 390, 96), (1000, 32768, 128),
+                                   (50, 2560, 1024), (50, 8192, 1024), (50, 1024, 2048),
+                                   (100, 160, 200), (8, 384, 128), (1, 3072, 1024)])
 def test_linear_matches_torch_fp32(rt, engine, m, n, k):
     if engine == 2 and k % 32:
         pytest.skip("warp-level engine needs K % 32 == 0")
+    if engine == 3 and (m > 128 or k > 16 * 4 * 64):
+        pytest.skip("weight-streaming engine: M <= 128, K <= 4096")
+    if engine == 1 and m < 128:
+        pytest.skip("tile engine: M >= 128")
     g = torch.Generator(device="cuda").manual_seed(m * 7 + n + k)
     x = torch.randn((m, k), generator=g, device="cuda").half()
     w = (0.05 * torch.randn((n, k), generator=g, device="cuda")).half()
