@@ -132,6 +132,11 @@ int pi0_linear(pi0_ctx* ctx, const void* x, int M, int K, const void* w, int N, 
  * bounded wait inside a kernel gave up. */
 int pi0_device_error(pi0_ctx* ctx);
 
+/* out[i] = a[i] / b[i] (fp32, n elements, device pointers) computed by the reciprocal-and-
+ * correction sequence the norm-fused projections use for x / sqrt(mean(x²) + eps); exposed so
+ * tests can compare it with IEEE division bit for bit. Context-free. */
+int pi0_div_check(const float* a, const float* b, float* out, int64_t n, pi0_stream_t stream);
+
 
 /* Kernels this context has launched so far (a replayed graph counts its kernel nodes). */
 int64_t pi0_launch_count(const pi0_ctx* ctx);

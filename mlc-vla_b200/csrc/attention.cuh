@@ -34,7 +34,7 @@ struct AttnArgs {
   const T* vB;
   int LB;
   int Tq, H, KV;
-  int keys_per_split;  // multiple of ATT_BK
+  int keys_per_split;  // multiple of the key tile width
   T* out;              // [B, Tq, H·hd]
   int a_is_ready;      // segment A was written before the previous kernel (the prefix cache
                        // during denoise): its tiles may be requested before griddepcontrol.wait
@@ -43,15 +43,15 @@ struct AttnArgs {
 constexpr int ATT_BQ = 64;   // query rows per CTA (4 warps × 16)
 constexpr int ATT_BK = 32;   // keys per tile
 
-template <int HD>
+template <int HD, int BK = ATT_BK>
 struct AttnSmem {
   static constexpr int QLD = HD + 4;   // fp32 row stride (conflict-free tf32 fragment loads)
   static constexpr int KLD = HD + 4;
   static constexpr int VLD = HD + 8;   // 16-bit row stride (conflict-free ldmatrix.trans)
   static constexpr int Q_BYTES = ATT_BQ * QLD * 4;
-  static constexpr int K_BYTES = ATT_BK * KLD * 4;
-  static constexpr int V_BYTES = ATT_BK * VLD * 2;
-  static constexpr int STAGE = K_BYTES + V_BYTES + ATT_BK * 4;
+  static constexpr int K_BYTES = BK * KLD * 4;
+  static constexpr int V_BYTES = BK * VLD * 2;
+  static constexpr int STAGE = K_BYTES + V_BYTES + BK * 4;
   static constexpr int BYTES = Q_BYTES + 2 * STAGE;
   // after the key loop: partial O [64][HD + 4] fp32 and (m, l) [64][2] reuse the same space
   static constexpr int OLD = HD + 4;
@@ -78,9 +78,10 @@ __device__ __forceinline__ float2 attn_ld2(uint32_t addr) {
   return v;
 }
 
-template <typename T, int HD>
+template <typename T, int HD, int BK>
 __global__ void __launch_bounds__(128) attn_kernel(AttnArgs<T> a) {
-  using SM = AttnSmem<HD>;
+  using SM = AttnSmem<HD, BK>;
+  constexpr int NT8 = BK / 8, NK16 = BK / 16;  // score n-tiles, PV k-steps per key tile
   extern __shared__ __align__(16) unsigned char smem_raw[];
   float* sQ = reinterpret_cast<float*>(smem_raw);
   auto sK = [&](int s) { return reinterpret_cast<float*>(smem_raw + SM::Q_BYTES + s * SM::STAGE); };
@@ -101,7 +102,7 @@ __global__ void __launch_bounds__(128) attn_kernel(AttnArgs<T> a) {
   const int Ltot = a.LA + a.LB;
   const int kbeg = split * a.keys_per_split;
   const int kend = min(Ltot, kbeg + a.keys_per_split);
-  const int ntiles = max(0, (kend - kbeg + ATT_BK - 1) / ATT_BK);
+  const int ntiles = max(0, (kend - kbeg + BK - 1) / BK);
 
   const float* kA = a.kA + ((size_t)b * a.KV + kvh) * a.LA * HD;
   const T* vA = a.vA + ((size_t)b * a.KV + kvh) * a.LA * HD;
@@ -109,25 +110,25 @@ __global__ void __launch_bounds__(128) attn_kernel(AttnArgs<T> a) {
   const T* vB = a.vB ? a.vB + ((size_t)b * a.KV + kvh) * a.LB * HD : nullptr;
   const float* mA = a.maskA ? a.maskA + (size_t)b * a.LA : nullptr;
 
-  // K/V tile of keys [k0, k0 + 32) into stage s (zero-filled past kend)
+  // K/V tile of keys [k0, k0 + BK) into stage s (zero-filled past kend)
   auto load_tile = [&](int s, int k0) {
     float* dk = sK(s);
     T* dv = sV(s);
-    for (int i = tid; i < ATT_BK * (HD / 4); i += 128) {
+    for (int i = tid; i < BK * (HD / 4); i += 128) {
       const int r = i / (HD / 4), ch = i % (HD / 4);
       const int key = k0 + r;
       const bool ok = key < kend;
       const float* src = ok ? (key < a.LA ? kA + (size_t)key * HD : kB + (size_t)(key - a.LA) * HD) : kA;
       cp_async16(dk + r * SM::KLD + ch * 4, src + (ok ? ch * 4 : 0), ok ? 16 : 0);
     }
-    for (int i = tid; i < ATT_BK * (HD / 8); i += 128) {
+    for (int i = tid; i < BK * (HD / 8); i += 128) {
       const int r = i / (HD / 8), ch = i % (HD / 8);
       const int key = k0 + r;
       const bool ok = key < kend;
       const T* src = ok ? (key < a.LA ? vA + (size_t)key * HD : vB + (size_t)(key - a.LA) * HD) : vA;
       cp_async16(dv + r * SM::VLD + ch * 8, src + (ok ? ch * 8 : 0), ok ? 16 : 0);
     }
-    if (tid < ATT_BK) {
+    if (tid < BK) {
       const int key = k0 + tid;
       float mv;
       if (key >= kend) mv = -1e30f;                   // outside this split: contributes 0
@@ -139,7 +140,7 @@ __global__ void __launch_bounds__(128) attn_kernel(AttnArgs<T> a) {
 
   // tiles made only of cached prefix keys (and their mask) are independent of the previous
   // kernel: start the first one before waiting on it
-  const bool t0_independent = a.a_is_ready && ntiles > 0 && kbeg + ATT_BK <= a.LA;
+  const bool t0_independent = a.a_is_ready && ntiles > 0 && kbeg + BK <= a.LA;
   if (t0_independent) load_tile(0, kbeg);
   cp_async_commit();
   pdl_trigger();
@@ -167,7 +168,7 @@ __global__ void __launch_bounds__(128) attn_kernel(AttnArgs<T> a) {
 
   for (int t = 0; t < ntiles; ++t) {
     const int s = t & 1;
-    if (t + 1 < ntiles) load_tile(s ^ 1, kbeg + (t + 1) * ATT_BK);  // prefetch the next tile
+    if (t + 1 < ntiles) load_tile(s ^ 1, kbeg + (t + 1) * BK);  // prefetch the next tile
     cp_async_commit();
     cp_async_wait<1>();  // everything but the just-issued prefetch has landed
     __syncthreads();
@@ -175,10 +176,10 @@ __global__ void __launch_bounds__(128) attn_kernel(AttnArgs<T> a) {
     const T* vt = sV(s);
     const float* mt = sMask(s);
 
-    // S = Q K^T for this warp's 16 rows × 32 keys
-    float sc[4][4];
+    // S = Q K^T for this warp's 16 rows × BK keys
+    float sc[NT8][4];
 #pragma unroll
-    for (int n = 0; n < 4; ++n) sc[n][0] = sc[n][1] = sc[n][2] = sc[n][3] = 0.f;
+    for (int n = 0; n < NT8; ++n) sc[n][0] = sc[n][1] = sc[n][2] = sc[n][3] = 0.f;
     const float* qw = sQ + (warp * 16) * SM::QLD;
 #pragma unroll 4
     for (int kk = 0; kk < HD; kk += 8) {
@@ -188,7 +189,7 @@ __global__ void __launch_bounds__(128) attn_kernel(AttnArgs<T> a) {
       af[2] = to_tf32(qw[gq * SM::QLD + kk + tq + 4]);
       af[3] = to_tf32(qw[(gq + 8) * SM::QLD + kk + tq + 4]);
 #pragma unroll
-      for (int n = 0; n < 4; ++n) {
+      for (int n = 0; n < NT8; ++n) {
         uint32_t bf[2];
         bf[0] = to_tf32(kt[(n * 8 + gq) * SM::KLD + kk + tq]);
         bf[1] = to_tf32(kt[(n * 8 + gq) * SM::KLD + kk + tq + 4]);
@@ -198,7 +199,7 @@ __global__ void __launch_bounds__(128) attn_kernel(AttnArgs<T> a) {
     // mask, online softmax
     float mx[2] = {m_r[0], m_r[1]};
 #pragma unroll
-    for (int n = 0; n < 4; ++n) {
+    for (int n = 0; n < NT8; ++n) {
       const float mk0 = mt[n * 8 + tq * 2], mk1 = mt[n * 8 + tq * 2 + 1];
       sc[n][0] += mk0;
       sc[n][1] += mk1;
@@ -215,9 +216,9 @@ __global__ void __launch_bounds__(128) attn_kernel(AttnArgs<T> a) {
     float corr[2], rs[2] = {0.f, 0.f};
 #pragma unroll
     for (int h = 0; h < 2; ++h) corr[h] = expf(m_r[h] - mx[h]);
-    uint32_t pf[2][4];  // P as two m16n8k16 A fragments (keys 0-15, 16-31)
+    uint32_t pf[NK16][4];  // P as m16n8k16 A fragments (16 keys each)
 #pragma unroll
-    for (int n = 0; n < 4; ++n) {
+    for (int n = 0; n < NT8; ++n) {
       const float p0 = expf(sc[n][0] - mx[0]), p1 = expf(sc[n][1] - mx[0]);
       const float p2 = expf(sc[n][2] - mx[1]), p3 = expf(sc[n][3] - mx[1]);
       rs[0] += p0 + p1;
@@ -242,7 +243,7 @@ __global__ void __launch_bounds__(128) attn_kernel(AttnArgs<T> a) {
     }
     // O += P V
 #pragma unroll
-    for (int kt2 = 0; kt2 < 2; ++kt2) {
+    for (int kt2 = 0; kt2 < NK16; ++kt2) {
 #pragma unroll
       for (int i = 0; i < HD / 8; i += 2) {
         uint32_t b0, b1, b2, b3;

@@ -132,6 +132,26 @@ __device__ __forceinline__ float gelu_tanh_f(float x) {
 }
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
 
+// L1 prefetch hint for an epilogue operand that is read later in the kernel
+__device__ __forceinline__ void pf_l1(const void* p) {
+  asm volatile("prefetch.global.L1 [%0];" ::"l"(p));
+}
+
+// a / b, correctly rounded, given rb = the correctly rounded reciprocal of b (__frcp_rn(b)):
+// q0 = RN(a·rb) is within one ulp of a/b, the remainder a − q0·b is exact in one fma, and the
+// corrected RN(q0 + rem·rb) equals RN(a/b) (Markstein's theorem; P. Markstein, "Computation of
+// elementary functions on the IBM RISC System/6000 processor", IBM J. R&D 34(1), 1990). Valid
+// for normal, finite operands without overflow or underflow, i.e. the RMS-norm quotient x / den
+// with den = sqrt(mean(x²) + eps) ≥ sqrt(eps). A zero, infinite or NaN first quotient (x = ±0,
+// ±inf or NaN) is returned as it is, which keeps IEEE division's signed zero and specials. A few
+// instructions instead of the general division sequence; pi0_div_check compares it with IEEE
+// division bit for bit.
+__device__ __forceinline__ float div_by_rcp(float a, float b, float rb) {
+  const float q0 = __fmul_rn(a, rb);
+  const float rem = fmaf(-q0, b, a);
+  return (fabsf(q0) < INFINITY && q0 != 0.f) ? fmaf(rem, rb, q0) : q0;
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

@@ -35,6 +35,9 @@ struct EpiStore {
   int ldo;
   const T* bias;
   int silu = 0;
+  __device__ void prefetch(int, int c) const {
+    if (bias) pf_l1(bias + c);
+  }
   __device__ void operator()(int r, int c, float v0, float v1) const {
     float a = Tr<T>::r(v0), b = Tr<T>::r(v1);
     if (bias) {
@@ -53,6 +56,7 @@ template <typename T>
 struct EpiResid {  // prefix residual (gemma_dual.py:338,340): x = round(x + round(acc))
   T* x;
   int ldx;
+  __device__ void prefetch(int r, int c) const { pf_l1(x + (size_t)r * ldx + c); }
   __device__ void operator()(int r, int c, float v0, float v1) const {
     T* p = x + (size_t)r * ldx + c;
     float a = Tr<T>::f(p[0]) + Tr<T>::r(v0);
@@ -68,6 +72,10 @@ struct EpiGatedResid {  // suffix residual (gemma_dual.py:91-94): x = round(x + 
   const T* gate;      // [rows_per_gate_group ...]: gate[(r / rows_per_gate) * gate_stride + c]
   int rows_per_gate;  // rows that share one gate vector (S·B when the time is shared)
   int gate_stride;
+  __device__ void prefetch(int r, int c) const {
+    pf_l1(x + (size_t)r * ldx + c);
+    pf_l1(gate + (size_t)(r / rows_per_gate) * gate_stride + c);
+  }
   // returns the new (rounded) x values, from which the next norm's Σx² partials are formed
   __device__ float2 operator()(int r, int c, float v0, float v1) const {
     const T* g = gate + (size_t)(r / rows_per_gate) * gate_stride + c;
@@ -86,6 +94,7 @@ template <typename T>
 struct EpiGeglu {
   T* h;
   int ldh;
+  __device__ void prefetch(int, int) const {}
   __device__ void operator()(int r, int c, float v0, float v1) const {
     float g = Tr<T>::r(gelu_tanh_f(Tr<T>::r(v0)));
     h[(size_t)r * ldh + (c >> 1)] = Tr<T>::t(g * Tr<T>::r(v1));
@@ -111,6 +120,16 @@ struct EpiQkvRope {
   int H, KV, hd;
   int col0;      // global column offset of this launch (skip q rows for the last prefill layer)
   float qscale;
+  __device__ void prefetch(int r, int c_local) const {
+    const int c = c_local + col0;
+    if (c < (H + KV) * hd) {
+      const int cc = c < H * hd ? c : c - H * hd;
+      const int b = r / T_len, pos = r - b * T_len;
+      const size_t t = (size_t)b * cs_bstride + (size_t)pos * (hd >> 1) + ((cc % hd) >> 1);
+      pf_l1(cos + t);
+      pf_l1(sin + t);
+    }
+  }
   __device__ void operator()(int r, int c_local, float v0, float v1) const {
     int c = c_local + col0;
     int hq = H * hd, hkv = KV * hd;

@@ -1,23 +1,33 @@
 // Weight-streaming GEMM for the denoise step (M = B·S activation rows ≤ 128, e.g. 50):
 //   Y[M, N] = X[M, K] · W[N, K]^T  with the fused epilogue functors of gemm_mma.cuh.
 //
-// The M=50 projections are HBM-bound (every weight byte is used 50 times), so the kernel is
-// built around streaming W once at full bandwidth:
+// The M=50 projections are HBM-bound (every weight byte is used M times), so the kernel is
+// built around streaming W once at full bandwidth while staying small enough that the CTAs of
+// two consecutive kernels fit on one SM together:
 //   * the weights are pre-packed (at pi0_set_params) into 16 KB blocks, one per (128-row tile,
 //     64-wide k-block), each already the 128-byte-swizzled K-major shared-memory image, and a
-//     tile's k-blocks are contiguous: a CTA pulls its whole weight slice with one-dimensional
-//     cp.async.bulk copies — sequential DRAM streams, no tensor map;
+//     tile's k-blocks are contiguous: a CTA streams its weight slice with one-dimensional
+//     cp.async.bulk copies — sequential DRAM, no tensor map;
 //   * swap-AB on tcgen05: the weight tile is the MMA's A operand (M = 128 weight rows) and the
 //     activations are B (N = NA = 64 or 128 rows, zero past M), accumulator [128 × NA] fp32 in
 //     TMEM;
-//   * split-K over a thread-block cluster of C CTAs (C ≤ 16): rank r owns k-blocks
+//   * a RING-deep shared-memory pipeline (weight block + activation block per stage) with
+//     warp-specialised roles: warp 0 streams blocks (weights by bulk copy, activations by TMA),
+//     warp 1 issues the MMAs and frees stages with tcgen05.commit, warps 2-5 normalise the
+//     activation blocks in place (NORM) and run the epilogue. Shared memory does not grow with
+//     K: ~100 KB per CTA, two CTAs per SM;
+//   * the epilogue's global operands are prefetched into L1 right after the dependency wait;
+//   * split-K over a thread-block cluster of C ≤ 8 CTAs: rank r owns k-blocks
 //     [r·kbpc, (r+1)·kbpc) of one tile; partial accumulators are summed through distributed
 //     shared memory in rank order (deterministic), each rank finishing 128/C weight rows;
-//   * programmatic dependent launch: the weight copies are issued before griddepcontrol.wait,
-//     so a kernel's weight stream overlaps the tail of the kernel producing its activations;
+//   * programmatic dependent launch: the first RING weight blocks are requested before
+//     griddepcontrol.wait, so a kernel's weight stream overlaps the kernel producing its
+//     activations;
 //   * optional fusions: NORM builds B = adaRMSNorm(x) in shared memory from the residual stream
 //     and per-row Σx² partials; SSQ makes the residual epilogue emit those partials (one per
-//     128-row tile, deterministic) for the next norm-fused GEMM.
+//     (tile, rank), deterministic) for the next norm-fused GEMM.
+// Every mbarrier wait is bounded (gemm_tc.cuh: mbar_wait); on timeout the kernel sets *err,
+// waits for the copies it issued, and frees TMEM before returning.
 #pragma once
 
 #include "gemm_tc.cuh"
@@ -49,11 +59,6 @@ __device__ __forceinline__ float4 ld_cluster4(uint32_t addr) {
                : "memory");
   return v;
 }
-__device__ __forceinline__ float ld_cluster1(uint32_t addr) {
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
-  return v;
-}
 // one-dimensional bulk copy global -> this CTA's shared memory, completing on an mbarrier
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile(
@@ -62,24 +67,30 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
       "l"(src), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
 }
+// barrier among the 128 threads of warps 2-5 (activation producers / epilogue)
+__device__ __forceinline__ void workers_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
-constexpr int KBPC_MAX = 4;           // k-blocks (of 64) per CTA
+constexpr int RING = 4;               // pipeline stages
 constexpr int W_BLOCK = BM * BK * 2;  // 16 KB: one packed (tile, k-block) weight block
 constexpr int PLD = BM + 4;           // partial row stride (floats): activation-row major
-constexpr int NORM_ITEMS = 4;         // 16-byte chunks a thread normalises per batch
+constexpr int MAX_C = 8;              // cluster size limit (portable clusters)
+constexpr int SSQ_MAX_PARTS = 256;    // row Σx² partials per row (multiple of 16)
+constexpr int NT = 192;               // threads per CTA
 
 template <int NA>
 struct SkSmem {
   static constexpr int X_BLOCK = NA * BK * 2;
-  static constexpr int LOAD = KBPC_MAX * (W_BLOCK + X_BLOCK);
-  static constexpr int PART = NA * PLD * 4;
-  static constexpr int BYTES = (LOAD > PART ? LOAD : PART) + 1024;
+  static constexpr int STAGE = W_BLOCK + X_BLOCK;  // multiple of 1024 (swizzle atoms)
+  static constexpr int LOAD = RING * STAGE;
+  static constexpr int PART = NA * PLD * 4;        // after the MMAs: partial accumulator
+  static constexpr int ITEM = NA * 32 * 4;         // after the MMAs: SSQ per-item squares
+  static constexpr int BYTES = (LOAD > PART + ITEM ? LOAD : PART + ITEM) + 1024;
 };
 
 struct SkArgs {
   int M, N, K;
-  int kbpc;              // k-blocks per CTA (≤ KBPC_MAX)
-  int C;                 // cluster size = number of K splits
+  int kbpc;              // k-blocks per CTA
+  int C;                 // cluster size = number of K splits (power of two ≤ MAX_C)
   int* err;
   const void* wpack;     // pre-packed weights, or null to load W through the tensor map
   // NORM: B = x / sqrt(Σx²/K + eps) · (1 + scale) + shift, (scale, shift) = mod[0:K], mod[K:2K]
@@ -87,7 +98,8 @@ struct SkArgs {
   const void* mod;       // modulation row of this step
   float eps;
   const float* ssq_in;   // [M][ssq_parts] partial Σx² of the rows of x
-  // SSQ: ssq_out[m][tile] = Σ over the tile's 128 features of x_new² (epilogue return values)
+  // SSQ: ssq_out[m][tile·C + rank] = Σ over the rank's output columns of x_new² (the values
+  // the epilogue returns); CTA (0, 0) zeroes the slots [tiles·C, ssq_parts)
   float* ssq_out;
   int ssq_parts;
 };
@@ -112,108 +124,85 @@ __global__ void pack_sw128_kernel(uint16_t* __restrict__ dst, const uint16_t* __
   *reinterpret_cast<uint4*>(dst + ((t * nkb + kb) * BM + r) * BK + cs * 8) = v;
 }
 
-// NORM prologue: writes this CTA's k-blocks of B = adaRMSNorm(x) into the swizzled smem operand.
+// NORM: normalises one raw x block in place. The block holds x[0:NA, 64 columns] as written by
+// TMA in the 128-byte swizzle layout (element (r, k) at r·128 + ((k/8) ^ (r & 7))·16 + (k%8)·2,
+// rows ≥ M and columns ≥ K zero-filled). Worker thread wt (0..127) owns 16-byte column chunk
+// q = wt & 7 of rows (wt >> 3) + 16·u; (sc, sh) are that chunk's 8 scale / shift values.
+//   B = RN16( RN(RN(x / den) · RN(1 + scale)) + shift ),  den = sqrt(Σx²/K + eps)
+// (gemma_dual.py:76-88, fp32 arithmetic, one rounding per operation).
 template <typename T, int NA>
-__device__ __forceinline__ void norm_to_smem(const SkArgs& a, uint8_t* sX, int kb0, int nk,
-                                             float* s_den) {
-  const int tid = threadIdx.x, nt = blockDim.x;
-  for (int m = tid; m < a.M; m += nt) {
-    const float* p = a.ssq_in + (size_t)m * a.ssq_parts;
-    float v[32];
+__device__ __forceinline__ void norm_inplace(const SkArgs& a, uint8_t* xb, uint4 sc, uint4 sh,
+                                             const float* s_den, const float* s_rcp, int wt) {
+  const int q = wt & 7;
+  const T* es = reinterpret_cast<const T*>(&sc);
+  const T* eh = reinterpret_cast<const T*>(&sh);
+  float s1[8], shf[8];
 #pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] = i < a.ssq_parts ? p[i] : 0.f;  // loads issued together
-    float ss = 0.f;
-#pragma unroll
-    for (int i = 0; i < 32; ++i) ss += v[i];
-    s_den[m] = sqrtf(__fadd_rn(__fdiv_rn(ss, (float)a.K), a.eps));
+  for (int e = 0; e < 8; ++e) {
+    s1[e] = __fadd_rn(1.f, Tr<T>::f(es[e]));
+    shf[e] = Tr<T>::f(eh[e]);
   }
-  __syncthreads();
-  const T* x = reinterpret_cast<const T*>(a.x);
-  const T* mod = reinterpret_cast<const T*>(a.mod);
-  const int cpr = nk * 8;  // 16-byte chunks per row in this CTA
-  const int total = NA * cpr;
-  const int c0 = kb0 * 8;
-  for (int base = tid; base < total; base += nt * NORM_ITEMS) {
-    uint4 xv[NORM_ITEMS], sc[NORM_ITEMS], sh[NORM_ITEMS];
+#pragma unroll 1
+  for (int u = 0; u < NA / 16; ++u) {
+    const int r = (wt >> 3) + 16 * u;
+    if (r >= a.M) break;  // zero rows stay zero
+    uint4* p = reinterpret_cast<uint4*>(xb + r * 128 + ((q ^ (r & 7)) << 4));
+    const uint4 v = *p;
+    const T* e = reinterpret_cast<const T*>(&v);
+    const float den = s_den[r], rcp = s_rcp[r];
+    uint32_t o[4];
 #pragma unroll
-    for (int u = 0; u < NORM_ITEMS; ++u) {
-      const int it = base + u * nt;
-      if (it >= total) continue;
-      const int r = it / cpr, c = c0 + it % cpr;
-      if (r < a.M) {
-        xv[u] = *reinterpret_cast<const uint4*>(x + (size_t)r * a.K + c * 8);
-        sc[u] = *reinterpret_cast<const uint4*>(mod + c * 8);
-        sh[u] = *reinterpret_cast<const uint4*>(mod + a.K + c * 8);
-      }
+    for (int j = 0; j < 4; ++j) {
+      const float n0 = div_by_rcp(Tr<T>::f(e[2 * j]), den, rcp);
+      const float n1 = div_by_rcp(Tr<T>::f(e[2 * j + 1]), den, rcp);
+      o[j] = Tr<T>::pack(__fadd_rn(__fmul_rn(n0, s1[2 * j]), shf[2 * j]),
+                         __fadd_rn(__fmul_rn(n1, s1[2 * j + 1]), shf[2 * j + 1]));
     }
-#pragma unroll
-    for (int u = 0; u < NORM_ITEMS; ++u) {
-      const int it = base + u * nt;
-      if (it >= total) continue;
-      const int r = it / cpr, cl = it % cpr;
-      uint4 outv = make_uint4(0, 0, 0, 0);
-      if (r < a.M) {
-        const float den = s_den[r];
-        const T* e = reinterpret_cast<const T*>(&xv[u]);
-        const T* es = reinterpret_cast<const T*>(&sc[u]);
-        const T* eh = reinterpret_cast<const T*>(&sh[u]);
-        uint32_t o[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          float v2[2];
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const int q = 2 * j + h;
-            const float n = __fdiv_rn(Tr<T>::f(e[q]), den);
-            v2[h] = __fadd_rn(__fmul_rn(n, __fadd_rn(1.f, Tr<T>::f(es[q]))), Tr<T>::f(eh[q]));
-          }
-          o[j] = Tr<T>::pack(v2[0], v2[1]);
-        }
-        outv = make_uint4(o[0], o[1], o[2], o[3]);
-      }
-      const int kb = cl >> 3, q = cl & 7;
-      *reinterpret_cast<uint4*>(sX + kb * (NA * BK * 2) + r * 128 + ((q ^ (r & 7)) << 4)) = outv;
-    }
+    *p = make_uint4(o[0], o[1], o[2], o[3]);
   }
   // generic-proxy smem writes -> visible to the tensor core (async proxy)
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 template <typename T, int NA, bool NORM, bool SSQ, class Epi>
-__global__ void __launch_bounds__(128) skinny_kernel(const __grid_constant__ CUtensorMap tmW,
-                                                     const __grid_constant__ CUtensorMap tmX,
-                                                     SkArgs a, Epi epi) {
+__global__ void __launch_bounds__(NT, 2) skinny_kernel(const __grid_constant__ CUtensorMap tmW,
+                                                       const __grid_constant__ CUtensorMap tmX,
+                                                       SkArgs a, Epi epi) {
   using S = SkSmem<NA>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
-  __shared__ __align__(8) uint64_t bar_w, bar_x, bar_mma;
+  // full_w / full_x: TMA landed; ready_x (NORM): block normalised; empty: MMAs done with a stage
+  __shared__ __align__(8) uint64_t full_w[RING], full_x[RING], ready_x[RING], empty[RING], bar_mma;
   __shared__ uint32_t s_tmem;
-  __shared__ int s_ok;
-  __shared__ float s_small[NA];                // NORM: row denominators; SSQ: rank partials
-  __shared__ float s_item[SSQ ? NA * 32 : 1];  // SSQ: per-item squares
+  __shared__ int s_ok, s_stop;
+  __shared__ float s_den[NORM ? NA : 1], s_rcp[NORM ? NA : 1];  // NORM: row sqrt(ms + eps), 1/it
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int C = a.C;
-  const uint32_t rank = C > 1 ? cluster_rank() : 0;
+  const uint32_t rank = cluster_rank();  // 0 for a cluster of one
   const int tile = blockIdx.x / C;
   const int n0 = tile * BM;
   const int nkb = (a.K + BK - 1) / BK;
   const int kb0 = rank * a.kbpc;
   const int nk = max(0, min(nkb, kb0 + a.kbpc) - kb0);
-  uint8_t* sW = base;
-  uint8_t* sX = base + KBPC_MAX * W_BLOCK;
-  float* part = reinterpret_cast<float*>(base);  // reused after the MMAs: [NA][PLD]
+  auto stage_w = [&](int s) { return base + s * S::STAGE; };
+  auto stage_x = [&](int s) { return base + s * S::STAGE + W_BLOCK; };
 
   if (tid == 0) {
-    mbar_init(&bar_w, 1);
-    mbar_init(&bar_x, 1);
+    for (int s = 0; s < RING; ++s) {
+      mbar_init(&full_w[s], 1);
+      mbar_init(&full_x[s], 1);
+      mbar_init(&ready_x[s], 1);
+      mbar_init(&empty[s], 1);
+    }
     mbar_init(&bar_mma, 1);
+    s_stop = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     if (!a.wpack) tma_prefetch_desc(&tmW);
-    if (!NORM) tma_prefetch_desc(&tmX);
+    tma_prefetch_desc(&tmX);
   }
-  if (warp == 0) {
+  if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(&s_tmem)),
                  "r"((uint32_t)NA));
@@ -224,142 +213,201 @@ __global__ void __launch_bounds__(128) skinny_kernel(const __grid_constant__ CUt
   tc_fence_after();
   const uint32_t tmem = s_tmem;
 
-  // weights never depend on the previous kernel: start streaming them before waiting on it
-  if (tid == 0 && nk > 0) {
-    mbar_expect_tx(&bar_w, nk * W_BLOCK);
-    if (a.wpack) {
-      const uint8_t* src = reinterpret_cast<const uint8_t*>(a.wpack) +
-                           ((size_t)tile * nkb + kb0) * W_BLOCK;
-      for (int i = 0; i < nk; ++i) bulk_load(sW + i * W_BLOCK, src + i * W_BLOCK, W_BLOCK, &bar_w);
-    } else {
-      for (int i = 0; i < nk; ++i) tma_load_2d(sW + i * W_BLOCK, &tmW, &bar_w, (kb0 + i) * BK, n0);
-    }
-  }
+  const uint8_t* wsrc =
+      a.wpack ? reinterpret_cast<const uint8_t*>(a.wpack) + ((size_t)tile * nkb + kb0) * W_BLOCK
+              : nullptr;
+  auto issue_w = [&](int i) {
+    const int s = i % RING;
+    mbar_expect_tx(&full_w[s], W_BLOCK);
+    if (wsrc) bulk_load(stage_w(s), wsrc + (size_t)i * W_BLOCK, W_BLOCK, &full_w[s]);
+    else tma_load_2d(stage_w(s), &tmW, &full_w[s], (kb0 + i) * BK, n0);
+  };
+
+  // weights never depend on the previous kernel: fill the ring before waiting on it
+  int issued = 0, issued_x = 0;  // thread 0: weight / activation blocks issued
+  if (tid == 0)
+    for (; issued < min(nk, RING); ++issued) issue_w(issued);
   pdl_trigger();
   pdl_wait();
-  if (NORM) {
-    if (nk > 0) norm_to_smem<T, NA>(a, sX, kb0, nk, s_small);
-    __syncthreads();
-  }
-  if (tid == 0) {
-    if (nk > 0) {
-      if (!NORM) {
-        mbar_expect_tx(&bar_x, nk * S::X_BLOCK);
-        for (int i = 0; i < nk; ++i)
-          tma_load_2d(sX + i * S::X_BLOCK, &tmX, &bar_x, (kb0 + i) * BK, 0);
-      }
-      bool ok = mbar_wait(&bar_w, 0, a.err, ERR_TIMEOUT_MMA, false) &&
-                (NORM || mbar_wait(&bar_x, 0, a.err, ERR_TIMEOUT_MMA, false));
-      if (ok) {
-        tc_fence_after();
-        constexpr uint32_t idesc = idesc_f16<T>(BM, NA);
-        for (int i = 0; i < nk; ++i) {
-          const uint64_t da = desc_sw128(smem_u32(sW + i * W_BLOCK));
-          const uint64_t db = desc_sw128(smem_u32(sX + i * S::X_BLOCK));
-#pragma unroll
-          for (int k = 0; k < BK / 16; ++k) umma_f16(tmem, da + 2 * k, db + 2 * k, idesc, (i | k) != 0);
+
+  // the epilogue's global operands (residual rows, gates, RoPE tables) do not depend on the
+  // accumulator: request them into L1 early, so the epilogue does not wait on L2 round trips
+  auto prefetch_epi = [&]() {
+    const int R = BM / C, quads = R / 4, total = quads * a.M;
+    for (int it = tid; it < total; it += NT) {
+      const int g = it % quads, m = it / quads;
+      const int n = n0 + rank * R + 4 * g;
+      if (n < a.N) epi.prefetch(m, n);
+    }
+  };
+
+  if (warp == 0) {
+    if (lane == 0) {  // producer: weight blocks past the first RING, all activation blocks
+      for (int i = 0; i < nk; ++i) {
+        const int s = i % RING;
+        if (i >= RING) {
+          if (!mbar_wait(&empty[s], ((i / RING) - 1) & 1, a.err, ERR_TIMEOUT_PRODUCER)) break;
+          issue_w(i);
+          issued = i + 1;
         }
+        mbar_expect_tx(&full_x[s], S::X_BLOCK);
+        tma_load_2d(stage_x(s), &tmX, &full_x[s], (kb0 + i) * BK, 0);
+        issued_x = i + 1;
       }
     }
-    umma_commit(&bar_mma);  // arrives once every issued MMA is done (at once if none)
-    s_ok = mbar_wait(&bar_mma, 0, a.err, ERR_TIMEOUT_EPI, false) ? 1 : 0;
+  } else if (warp == 1) {
+    if (lane == 0) {  // MMA issuer
+      constexpr uint32_t idesc = idesc_f16<T>(BM, NA);
+      for (int i = 0; i < nk; ++i) {
+        const int s = i % RING;
+        const uint32_t ph = (i / RING) & 1;
+        if (!mbar_wait(&full_w[s], ph, a.err, ERR_TIMEOUT_MMA) ||
+            !mbar_wait(NORM ? &ready_x[s] : &full_x[s], ph, a.err, ERR_TIMEOUT_MMA))
+          break;
+        tc_fence_after();
+        const uint64_t da = desc_sw128(smem_u32(stage_w(s)));
+        const uint64_t db = desc_sw128(smem_u32(stage_x(s)));
+#pragma unroll
+        for (int k = 0; k < BK / 16; ++k)
+          umma_f16(tmem, da + 2 * k, db + 2 * k, idesc, (i | k) != 0 ? 1u : 0u);
+        umma_commit(&empty[s]);
+      }
+      umma_commit(&bar_mma);  // arrives once every issued MMA is done (at once if none)
+    }
+  } else {
+    if (NORM) {  // warps 2-5: normalise each raw x block in place once its copy has landed
+      const int wt = tid - 64;
+      const T* mod = reinterpret_cast<const T*>(a.mod);
+      const uint4 z = make_uint4(0, 0, 0, 0);
+      auto load_mod = [&](int i, uint4& c1, uint4& c2) {
+        const int col = (kb0 + i) * BK + (wt & 7) * 8;
+        const bool in = col < a.K;
+        c1 = in ? *reinterpret_cast<const uint4*>(mod + col) : z;
+        c2 = in ? *reinterpret_cast<const uint4*>(mod + a.K + col) : z;
+      };
+      uint4 sc = z, sh = z;
+      if (nk > 0) load_mod(0, sc, sh);
+      if (wt < a.M) {  // M ≤ NA ≤ 128: one row per thread; partials summed in slot order
+        const float4* p = reinterpret_cast<const float4*>(a.ssq_in + (size_t)wt * a.ssq_parts);
+        float ss = 0.f;
+        for (int i = 0; i < a.ssq_parts / 4; i += 4) {
+          float4 v[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) v[j] = p[i + j];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) ss = ((ss + v[j].x) + v[j].y + v[j].z) + v[j].w;
+        }
+        const float den = sqrtf(__fadd_rn(__fdiv_rn(ss, (float)a.K), a.eps));
+        s_den[wt] = den;
+        s_rcp[wt] = __frcp_rn(den);
+      }
+      workers_sync();
+      for (int i = 0; i < nk; ++i) {
+        const int s = i % RING;
+        uint4 nsc = z, nsh = z;
+        if (i + 1 < nk) load_mod(i + 1, nsc, nsh);
+        if (!mbar_wait(&full_x[s], (i / RING) & 1, a.err, ERR_TIMEOUT_EPI)) s_stop = 1;
+        workers_sync();
+        if (s_stop) break;
+        norm_inplace<T, NA>(a, stage_x(s), sc, sh, s_den, s_rcp, wt);
+        workers_sync();
+        if (wt == 0) mbar_arrive(&ready_x[s]);
+        sc = nsc;
+        sh = nsh;
+      }
+    }
+  }
+  // one call site for every thread: idle lanes and, in NORM launches, the workers once their
+  // blocks are done (the epilogue is still about a microsecond away)
+  prefetch_epi();
+
+  // ---- accumulator -> shared memory partial ----
+  if (tid == 64) s_ok = mbar_wait(&bar_mma, 0, a.err, ERR_TIMEOUT_EPI, false) ? 1 : 0;
+  if (tid == 0) {
+    // drain: every copy this thread issued has landed before the ring memory is reused (the
+    // normal path consumed them all; this matters after a timeout)
+    for (int i = max(0, issued - RING); i < issued; ++i)
+      mbar_wait(&full_w[i % RING], (i / RING) & 1, a.err, ERR_TIMEOUT_PRODUCER, false);
+    for (int i = max(0, issued_x - RING); i < issued_x; ++i)
+        mbar_wait(&full_x[i % RING], (i / RING) & 1, a.err, ERR_TIMEOUT_PRODUCER, false);
   }
   __syncthreads();
-  const bool ok = s_ok != 0;
+  const bool ok = s_ok != 0 && nk > 0;
   tc_fence_after();
-  // accumulator -> shared partial part[act row][weight row] (weight row = TMEM lane)
-  const int wrow = warp * 32 + lane;
-  if (nk > 0 && ok) {
+  float* part = reinterpret_cast<float*>(base);  // [NA][PLD], aliases the drained ring
+  if (warp >= 2) {
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int wrow = q * 32 + lane;
 #pragma unroll 1
     for (int c = 0; c < NA; c += 32) {
       uint32_t v[32];
-      tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + c, v);
+      if (ok) {
+        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + c, v);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = 0u;
+      }
 #pragma unroll
       for (int j = 0; j < 32; ++j) part[(c + j) * PLD + wrow] = __uint_as_float(v[j]);
     }
-  } else {
-    for (int j = 0; j < NA; ++j) part[j * PLD + wrow] = 0.f;
   }
   tc_fence_before();
-  if (C > 1) cluster_sync();
-  else __syncthreads();
+  cluster_sync();
 
-  // rank r finishes weight rows [r·R, (r+1)·R) of the tile: each item is 4 consecutive weight
-  // rows of one activation row, read from all C ranks with 16-byte loads issued together and
-  // summed in rank order (deterministic)
+  // ---- split-K reduction + epilogue: rank r finishes weight rows [r·R, (r+1)·R) ----
+  // One (activation row, 4 weight rows) item per iteration, the C partials of an item loaded
+  // together, and a single call site of the epilogue: every CTA runs this code once, so it is
+  // kept short (instruction fetch, not arithmetic, bounds a cold one-pass epilogue).
   const int R = BM / C, quads = R / 4;
   const uint32_t pbase = smem_u32(part);
   const int total = quads * a.M;
-  const int lc = 31 - __clz(C);      // C is a power of two ≤ 16
-  const int ipb = 16 >> lc;          // items per batch: 16 loads in flight per thread
-  for (int base = tid; base < total; base += blockDim.x * ipb) {
-    float4 v[16];
+  float* s_item = reinterpret_cast<float*>(base + S::PART);
+#pragma unroll 1
+  for (int it = tid; it < total; it += NT) {
+    const int g = it % quads, m = it / quads;
+    const uint32_t off = pbase + (uint32_t)(m * PLD + rank * R + 4 * g) * 4u;
+    float4 v[MAX_C];
 #pragma unroll
-    for (int q = 0; q < 16; ++q) {
-      const int u = q >> lc, c = q & (C - 1);
-      const int it = base + u * blockDim.x;
-      v[q] = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (u < ipb && it < total) {
-        const int g = it % quads, m = it / quads;
-        const uint32_t off = pbase + (uint32_t)(m * PLD + rank * R + 4 * g) * 4u;
-        v[q] = ld_cluster4(C > 1 ? map_rank(off, c) : off);
+    for (int c = 0; c < MAX_C; ++c)
+      if (c < C) v[c] = ld_cluster4(map_rank(off, c));
+    float4 sum = v[0];
+#pragma unroll
+    for (int c = 1; c < MAX_C; ++c)
+      if (c < C) {
+        sum.x += v[c].x;
+        sum.y += v[c].y;
+        sum.z += v[c].z;
+        sum.w += v[c].w;
+      }
+    float sq = 0.f;
+    const int nb = n0 + rank * R + 4 * g;
+#pragma unroll 1
+    for (int h = 0; h < 2; ++h) {
+      const int n = nb + 2 * h;
+      if (n >= a.N) break;
+      const float v0 = h ? sum.z : sum.x, v1 = h ? sum.w : sum.y;
+      if constexpr (SSQ) {
+        const float2 p = epi(m, n, v0, v1);
+        sq += p.x * p.x + p.y * p.y;
+      } else {
+        epi(m, n, v0, v1);
       }
     }
-    // per item: sum its C partials in rank order (static register indices only)
-    float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-    for (int q = 0; q < 16; ++q) {
-      sum.x += v[q].x;
-      sum.y += v[q].y;
-      sum.z += v[q].z;
-      sum.w += v[q].w;
-      if ((q & (C - 1)) == C - 1) {
-        const int u = q >> lc;
-        const int it = base + u * blockDim.x;
-        if (u < ipb && it < total) {
-          const int g = it % quads, m = it / quads;
-          const int n = n0 + rank * R + 4 * g;
-          if constexpr (SSQ) {
-            float sq = 0.f;
-            if (n < a.N) {
-              const float2 p = epi(m, n, sum.x, sum.y);
-              sq += p.x * p.x + p.y * p.y;
-            }
-            if (n + 2 < a.N) {
-              const float2 p = epi(m, n + 2, sum.z, sum.w);
-              sq += p.x * p.x + p.y * p.y;
-            }
-            s_item[it] = sq;
-          } else {
-            if (n < a.N) epi(m, n, sum.x, sum.y);
-            if (n + 2 < a.N) epi(m, n + 2, sum.z, sum.w);
-          }
-        }
-        sum = make_float4(0.f, 0.f, 0.f, 0.f);
-      }
-    }
+    if constexpr (SSQ) s_item[it] = sq;
   }
   if constexpr (SSQ) {
     __syncthreads();
-    for (int m = tid; m < a.M; m += blockDim.x) {
+    const int parts_used = (int)gridDim.x;  // tiles · C
+    for (int m = tid; m < a.M; m += NT) {
       float q = 0.f;
       for (int g = 0; g < quads; ++g) q += s_item[m * quads + g];
-      s_small[m] = q;
-    }
-    if (C > 1) cluster_sync();
-    else __syncthreads();
-    if (rank == 0) {
-      const uint32_t sb = smem_u32(s_small);
-      for (int m = tid; m < a.M; m += blockDim.x) {
-        float q = 0.f;
-        for (int c = 0; c < C; ++c) q += ld_cluster1(C > 1 ? map_rank(sb + m * 4, c) : sb + m * 4);
-        a.ssq_out[(size_t)m * a.ssq_parts + tile] = q;
-      }
+      a.ssq_out[(size_t)m * a.ssq_parts + tile * C + rank] = q;
+      if (blockIdx.x == 0)
+        for (int p = parts_used; p < a.ssq_parts; ++p) a.ssq_out[(size_t)m * a.ssq_parts + p] = 0.f;
     }
   }
-  if (C > 1) cluster_sync();  // keep this CTA's shared memory alive until every rank has read it
-  __syncthreads();
-  if (warp == 0) {
+  cluster_sync();  // keep this CTA's shared memory alive until every rank has read it
+  if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
                  "r"((uint32_t)NA));

@@ -58,9 +58,8 @@ __device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
 // soon as another role has reported an error (unless `bail` is false: drain waits). The hot
 // loop only polls the barrier; the clock is read every 128 polls and the (global) error flag
 // every 8192, so a completed phase is seen without a memory round trip in the way.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code,
-                                          bool bail = true) {
-  if (mbar_try(bar, parity)) return true;
+__device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, int* err, int code,
+                                            bool bail) {
   const unsigned long long t0 = globaltimer();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try(bar, parity)) return true;
@@ -72,6 +71,13 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
       if (bail && (it & 8191) == 0 && *(volatile int*)err != 0) return false;
     }
   }
+}
+// (the polling loop is out of line: it is rarely entered more than once per wait, and keeping it
+// out of every call site keeps the kernels' code small)
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code,
+                                          bool bail = true) {
+  if (mbar_try(bar, parity)) return true;
+  return mbar_wait_slow(bar, parity, err, code, bail);
 }
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar,

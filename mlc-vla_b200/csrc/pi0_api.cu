@@ -371,15 +371,26 @@ int gemm(pi0_ctx* ctx, const T* A, int lda, const T* W, int ldw, int M, int N, i
          const Epi& epi, cudaStream_t st, int fam, int engine = 0);
 
 // Weight-streaming path for M ≤ 128 activation rows (see gemm_skinny.cuh). Cluster size C (the
-// K split) is the smallest power of two that keeps ≤ KBPC_MAX k-blocks per CTA and gives at
-// least 128 CTAs.
-int skinny_split(int N, int K) {
+// K split) is the smallest power of two ≤ 8 that gives at least 128 CTAs, as long as every CTA
+// keeps at least two k-blocks to stream; norm-fused launches also split until a CTA's blocks
+// fit the ring, so all of its raw activation blocks are requested at once.
+int skinny_split(int N, int K, bool norm) {
   const int nkb = (K + 63) / 64, tiles = (N + 127) / 128;
   int C = 1;
-  while (C < 16 && C < nkb &&
-         ((nkb + C - 1) / C > sk::KBPC_MAX || tiles * C < 128))
+  while (C < sk::MAX_C && nkb >= 4 * C &&
+         (tiles * C < 128 || (norm && (nkb + C - 1) / C > sk::RING)))
     C *= 2;
   return C;
+}
+
+// Row Σx² partial slots of the suffix residual stream: one per (tile, rank) of the widest
+// residual-producing projection (o_proj, down_proj), rounded up to a multiple of 16.
+int ssq_slots(const pi0_config& c) {
+  const int W1 = c.ae_width;
+  const int tiles = (W1 + 127) / 128;
+  const int p = tiles * std::max(skinny_split(W1, c.num_heads * c.head_dim, false),
+                                 skinny_split(W1, c.ae_mlp_dim, false));
+  return (p + 15) / 16 * 16;
 }
 
 struct SkOpt {
@@ -391,13 +402,12 @@ template <typename T, int NA, bool NORM, bool SSQ, class Epi>
 int skinny_launch(pi0_ctx* ctx, const T* X, int ldx, const T* W, int ldw, int M, int N, int K,
                   const Epi& epi, cudaStream_t st, int fam, SkOpt o) {
   const int nkb = (K + 63) / 64, tiles = (N + 127) / 128;
-  const int C = skinny_split(N, K);
+  const int C = skinny_split(N, K, NORM);
   const int kbpc = (nkb + C - 1) / C;
-  if (kbpc > sk::KBPC_MAX) return fail(ctx, PI0_ERR_UNSUPPORTED, "K too large for the weight-streaming GEMM");
-  if (NORM && (K % 8 || K > 4096 || ldx != K))
-    return fail(ctx, PI0_ERR_UNSUPPORTED, "norm-fused GEMM needs K % 8 == 0, K <= 4096, dense rows");
-  if (SSQ && tiles != ctx->ssq_parts)
-    return fail(ctx, PI0_ERR_INVALID, "row-sum partials: tile count differs from ssq_parts");
+  if (NORM && (K % 8 || ldx != K))
+    return fail(ctx, PI0_ERR_UNSUPPORTED, "norm-fused GEMM needs K % 8 == 0 and dense rows");
+  if (SSQ && tiles * C > ctx->ssq_parts)
+    return fail(ctx, PI0_ERR_INVALID, "row-sum partials: more (tile, rank) pairs than slots");
   CUtensorMap tw, tx;
   const bool bf = Tr<T>::kBf16;
   TRY(make_tmap(ctx, &tw, W, N, K, ldw, tc::BM, bf));
@@ -405,7 +415,7 @@ int skinny_launch(pi0_ctx* ctx, const T* X, int ldx, const T* W, int ldw, int M,
   sk::SkArgs a{M, N, K, kbpc, C, ctx->dev_err, o.wpack, X, o.mod, ctx->cfg.rms_norm_eps,
                ctx->ssq, ctx->ssq, ctx->ssq_parts};
   Prof pr(ctx, fam, st);
-  return launch(ctx, sk::skinny_kernel<T, NA, NORM, SSQ, Epi>, dim3(tiles * C), dim3(128),
+  return launch(ctx, sk::skinny_kernel<T, NA, NORM, SSQ, Epi>, dim3(tiles * C), dim3(sk::NT),
                 sk::SkSmem<NA>::BYTES, st, dim3(C, 1, 1), tw, tx, a, epi);
 }
 
@@ -493,15 +503,13 @@ int gemm(pi0_ctx* ctx, const T* A, int lda, const T* W, int ldw, int M, int N, i
 }
 
 // ---- attention launch ----------------------------------------------------------------------
-// Key splits (a power of two ≤ 16, so the splits of a row tile form one cluster): grow while
-// the grid stays within two waves over the SMs and every split keeps at least one key tile.
-int attn_splits(int rows, int batch, int KV, int ltot, int num_sms, bool allow_split) {
-  if (!allow_split) return 1;
+// Key splits (a power of two ≤ max_splits, so the splits of a row tile form one cluster): grow
+// while the grid stays within two waves over the SMs and every split keeps at least one key tile.
+int attn_splits(int rows, int batch, int KV, int ltot, int num_sms, int max_splits) {
   const int row_tiles = (rows + ATT_BQ - 1) / ATT_BQ;
   const int ctas = row_tiles * batch * KV;
   int splits = 1;
-  while (splits < 16 && ctas * splits * 2 <= 2 * num_sms &&
-         (ltot + splits * 2 * ATT_BK - 1) / (splits * 2 * ATT_BK) >= 1 &&
+  while (splits < max_splits && ctas * splits * 2 <= 2 * num_sms &&
          splits * 2 * ATT_BK <= ltot + ATT_BK)
     splits *= 2;
   return splits;
@@ -511,6 +519,8 @@ int attn_kps(int ltot, int splits) {
   return (kps + ATT_BK - 1) / ATT_BK * ATT_BK;
 }
 
+// The denoise step (segment A = the prefix cache, ready before the previous kernel) splits the
+// keys over up to 16 CTAs of one cluster; prefill has enough row tiles without splitting.
 template <typename T, int HD>
 int attn_launch_hd(pi0_ctx* ctx, AttnArgs<T> a, int batch, bool allow_split, cudaStream_t st,
                    int fam) {
@@ -518,10 +528,10 @@ int attn_launch_hd(pi0_ctx* ctx, AttnArgs<T> a, int batch, bool allow_split, cud
   const int G = a.H / a.KV, rows = a.Tq * G;
   const int row_tiles = (rows + ATT_BQ - 1) / ATT_BQ;
   const int ltot = a.LA + a.LB;
-  const int splits = attn_splits(rows, batch, a.KV, ltot, ctx->num_sms, allow_split);
+  const int splits = attn_splits(rows, batch, a.KV, ltot, ctx->num_sms, allow_split ? 16 : 1);
   a.keys_per_split = attn_kps(ltot, splits);
   dim3 grid(row_tiles, splits, batch * a.KV);
-  return launch(ctx, attn_kernel<T, HD>, grid, dim3(128), AttnSmem<HD>::BYTES, st,
+  return launch(ctx, attn_kernel<T, HD, ATT_BK>, grid, dim3(128), AttnSmem<HD, ATT_BK>::BYTES, st,
                 dim3(1, splits, 1), a);
 }
 
@@ -760,9 +770,10 @@ int attr_gemm_both(pi0_ctx* ctx) {
 }
 template <typename T, int HD>
 int attr_attn(pi0_ctx* ctx) {
-  CK(cudaFuncSetAttribute(attn_kernel<T, HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                          AttnSmem<HD>::BYTES));
-  CK(cudaFuncSetAttribute(attn_kernel<T, HD>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+  CK(cudaFuncSetAttribute(attn_kernel<T, HD, ATT_BK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                          AttnSmem<HD, ATT_BK>::BYTES));
+  CK(cudaFuncSetAttribute(attn_kernel<T, HD, ATT_BK>, cudaFuncAttributeNonPortableClusterSizeAllowed,
+                          1));
   return 0;
 }
 template <typename T>
@@ -944,7 +955,9 @@ int alloc_all(pi0_ctx* ctx) {
   TRY(dev_alloc(ctx, (void**)&ctx->tickets, (1 << 16) * 4));
   CK(cudaMemset(ctx->tickets, 0, (1 << 16) * 4));
   TRY(dev_alloc(ctx, (void**)&ctx->dev_err, 16));
-  ctx->ssq_parts = (int)((W1 + 127) / 128);
+  ctx->ssq_parts = ssq_slots(ctx->cfg);
+  if (ctx->ssq_parts > sk::SSQ_MAX_PARTS)
+    return fail(ctx, PI0_ERR_UNSUPPORTED, "action-expert width too large for the row-sum partials");
   TRY(dev_alloc(ctx, (void**)&ctx->ssq, MS * ctx->ssq_parts * 4));
   CK(cudaMemset(ctx->dev_err, 0, 16));
   return 0;
@@ -1313,6 +1326,13 @@ int pi0_linear(pi0_ctx* ctx, const void* x, int M, int K, const void* w, int N, 
   using T = __half;
   return gemm<T>(ctx, (const T*)x, K, (const T*)w, K, M, N, K, EpiStore<T>{(T*)y, N, nullptr},
                  stream, F_PRE_QKV, engine);
+}
+
+int pi0_div_check(const float* a, const float* b, float* out, int64_t n, pi0_stream_t stream) {
+  if (!a || !b || !out || n < 0) return PI0_ERR_INVALID;
+  if (n == 0) return 0;
+  div_check_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(a, b, out, n);
+  return cudaGetLastError() == cudaSuccess ? 0 : PI0_ERR_CUDA;
 }
 
 int pi0_device_error(pi0_ctx* ctx) {

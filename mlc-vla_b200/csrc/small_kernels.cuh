@@ -251,4 +251,11 @@ __global__ void dequantize_kernel(const uint32_t* __restrict__ qw, const T* __re
   w[id] = Tr<T>::t(((float)code - (float)maxint) * s);
 }
 
+// a / b through div_by_rcp (common.cuh), for the bit-for-bit comparison with IEEE division
+__global__ void div_check_kernel(const float* __restrict__ a, const float* __restrict__ b,
+                                 float* __restrict__ out, int64_t n) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) out[i] = div_by_rcp(a[i], b[i], __frcp_rn(b[i]));
+}
+
 }  // namespace pi0
