@@ -128,6 +128,22 @@ int pi0_dequantize_weight(int quant, int dtype, const uint32_t* q_weight, const 
 int pi0_linear(pi0_ctx* ctx, const void* x, int M, int K, const void* w, int N, void* y,
                int engine, pi0_stream_t stream);
 
+/* Allocation-free, context-free variant of pi0_linear's warp-level engine (engine 2); no
+ * counterpart in the reference. For callers that must not allocate device memory after start-up
+ * and may hold no pi0 context at all: a control loop with a fixed memory budget, or an embedder
+ * that owns every allocation itself. Same arguments as pi0_linear plus the model dtype
+ * (PI0_F16 / PI0_BF16); K must be a multiple of 32, N even.
+ * The split-K partials and tile tickets live in static device memory of this library (4 MiB of
+ * fp32 partials, 4096 tiles). The first call on a device looks up their addresses and the SM
+ * count with that device current (no allocation); make it before any stream capture. Returns
+ * PI0_ERR_UNSUPPORTED when a call would need more scratch than that (splits·M·N > 2^20 floats or
+ * more than 4096 output tiles). The tickets must be zero between calls: static memory starts
+ * zeroed and every call leaves them zero. The scratch is shared by all calls on a device, so
+ * calls that overlap in time (two streams or two threads) race on it and must be serialised by
+ * the caller. */
+int pi0_linear_noalloc(int dtype, const void* x, int M, int K, const void* w, int N, void* y,
+                       pi0_stream_t stream);
+
 /* Reads and clears the device error flag (synchronises the context's device). Nonzero means a
  * bounded wait inside a kernel gave up. */
 int pi0_device_error(pi0_ctx* ctx);

@@ -18,6 +18,7 @@
 #include <cstdio>
 #include <cstring>
 #include <map>
+#include <mutex>
 #include <string>
 #include <tuple>
 #include <vector>
@@ -1350,3 +1351,90 @@ const char* pi0_profile_family_name(int family) {
 }
 
 }  // extern "C"
+
+// ---- allocation-free projection ----------------------------------------------------------
+// y[M, N] = x[M, K] · w[N, K]^T on the warp-level split-K engine, with its split-K scratch in
+// static device memory instead of a context's workspace, so that a call allocates nothing.
+// The scratch is shared by every call on a device: calls that overlap in time (two streams,
+// two host threads) race on it, so a caller must serialise them.
+namespace {
+
+constexpr size_t kNoAllocWsFloats = size_t(1) << 20;  // 4 MiB of fp32 split-K partials
+constexpr int kNoAllocTickets = 4096;                  // output tiles of one call
+constexpr int kNoAllocMaxDevices = 64;
+
+// Tickets count the splits that have finished a tile; the last one resets its ticket to zero,
+// so they are zero between calls. Static device memory starts zeroed; nothing else has to.
+static __device__ __align__(256) float g_noalloc_ws[kNoAllocWsFloats];
+static __device__ __align__(256) int g_noalloc_tickets[kNoAllocTickets];
+
+struct NoAllocDev {
+  float* ws = nullptr;
+  int* tickets = nullptr;
+  int num_sms = 0;
+};
+NoAllocDev g_noalloc[kNoAllocMaxDevices];
+std::mutex g_noalloc_mu;
+
+// Once per device, with that device current: the device addresses of the static scratch and
+// the SM count. Neither call allocates.
+int noalloc_setup(NoAllocDev* out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return PI0_ERR_CUDA;
+  if (dev < 0 || dev >= kNoAllocMaxDevices) return PI0_ERR_DEVICE;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  NoAllocDev& d = g_noalloc[dev];
+  if (!d.ws) {
+    void* ws = nullptr;
+    void* tk = nullptr;
+    int sms = 0;
+    if (cudaGetSymbolAddress(&ws, g_noalloc_ws) != cudaSuccess) return PI0_ERR_CUDA;
+    if (cudaGetSymbolAddress(&tk, g_noalloc_tickets) != cudaSuccess) return PI0_ERR_CUDA;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+      return PI0_ERR_CUDA;
+    d.tickets = static_cast<int*>(tk);
+    d.num_sms = sms;
+    d.ws = static_cast<float*>(ws);
+  }
+  *out = d;
+  return 0;
+}
+
+template <typename T>
+int linear_noalloc(const NoAllocDev& d, const T* x, int M, int K, const T* w, int N, T* y,
+                   cudaStream_t st) {
+  using C = GemmCfg<T, 64, 64, 32, 32, 4>;
+  // the split rule of the context-owning warp-level engine (gemm(), M < 256)
+  const int tiles = ((M + 63) / 64) * ((N + 63) / 64);
+  int splits = std::max(1, (2 * d.num_sms + tiles - 1) / tiles);
+  splits = std::min(splits, std::max(1, K / 128));
+  const int ksteps = K / 32;
+  splits = std::max(1, std::min(splits, ksteps));
+  const int per = (ksteps + splits - 1) / splits;
+  splits = (ksteps + per - 1) / per;
+  if (splits > 1 && ((size_t)splits * M * N > kNoAllocWsFloats || tiles > kNoAllocTickets))
+    return PI0_ERR_UNSUPPORTED;
+  GemmArgs<T> g{x, K, w, K, M, N, K, per * 32, d.ws, d.tickets};
+  dim3 grid((N + 63) / 64, (M + 63) / 64, splits);
+  gemm_mma_kernel<T, 64, 64, 32, 32, 4, EpiStore<T>><<<grid, C::NT, C::SMEM, st>>>(
+      g, EpiStore<T>{y, N, nullptr});
+  return cudaGetLastError() == cudaSuccess ? 0 : PI0_ERR_CUDA;
+}
+
+}  // namespace
+
+int pi0_linear_noalloc(int dtype, const void* x, int M, int K, const void* w, int N, void* y,
+                       pi0_stream_t stream) {
+  if (!x || !w || !y || M < 1 || N < 2 || (N & 1) || K < 32 || (K % 32)) return PI0_ERR_INVALID;
+  if (dtype != PI0_F16 && dtype != PI0_BF16) return PI0_ERR_INVALID;
+  NoAllocDev d;
+  const int rc = noalloc_setup(&d);
+  if (rc) return rc;
+  if (dtype == PI0_BF16) {
+    using T = __nv_bfloat16;
+    return linear_noalloc<T>(d, (const T*)x, M, K, (const T*)w, N, (T*)y, stream);
+  }
+  using T = __half;
+  return linear_noalloc<T>(d, (const T*)x, M, K, (const T*)w, N, (T*)y, stream);
+}
+
