@@ -26,6 +26,27 @@ struct GemmArgs {
 };
 
 // ---- epilogues: operator()(row, col, v(col), v(col+1)); col is even ----
+// chunk32(row, col0, v[32]) is the same epilogue for 32 consecutive columns (col0 a multiple of
+// 32, all columns valid): every global operand of the chunk is loaded with 16-byte vectors before
+// any result is stored, so a read-modify-write epilogue costs one memory round trip per chunk
+// instead of one per column pair (a store to the array an operand is read from orders the next
+// load after it). It returns false, having done nothing, when a pointer is not 16-byte aligned;
+// the caller then runs operator() per pair.
+
+__device__ __forceinline__ bool al16(const void* p) {
+  return (reinterpret_cast<uintptr_t>(p) & 15) == 0;
+}
+template <typename T>
+__device__ __forceinline__ void ld16x4(const T* p, uint4 (&v)[4]) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) v[i] = reinterpret_cast<const uint4*>(p)[i];
+}
+template <typename T>
+__device__ __forceinline__ void st16x4(T* p, const uint4 (&v)[4]) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) reinterpret_cast<uint4*>(p)[i] = v[i];
+}
+
 
 // y = round(round(acc) + bias) (nn.Linear: matmul, then bias add; bias optional), then
 // optionally round(silu(y)) (the time MLP, pi0_model.py:106-109), stored in the model dtype.
@@ -50,6 +71,30 @@ struct EpiStore {
     }
     *reinterpret_cast<uint32_t*>(out + (size_t)r * ldo + c) = Tr<T>::pack(a, b);
   }
+  __device__ bool chunk32(int r, int c0, const float* v) const {
+    T* o = out + (size_t)r * ldo + c0;
+    if (!al16(o) || (bias && !al16(bias + c0))) return false;
+    uint4 bv[4];
+    if (bias) ld16x4(bias + c0, bv);
+    const T* be = reinterpret_cast<const T*>(bv);
+    uint4 ov[4];
+    uint32_t* ow = reinterpret_cast<uint32_t*>(ov);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      float a = Tr<T>::r(v[2 * j]), b = Tr<T>::r(v[2 * j + 1]);
+      if (bias) {
+        a = Tr<T>::r(a + Tr<T>::f(be[2 * j]));
+        b = Tr<T>::r(b + Tr<T>::f(be[2 * j + 1]));
+      }
+      if (silu) {
+        a = silu_f(a);
+        b = silu_f(b);
+      }
+      ow[j] = Tr<T>::pack(a, b);
+    }
+    st16x4(o, ov);
+    return true;
+  }
 };
 
 template <typename T>
@@ -62,6 +107,21 @@ struct EpiResid {  // prefix residual (gemma_dual.py:338,340): x = round(x + rou
     float a = Tr<T>::f(p[0]) + Tr<T>::r(v0);
     float b = Tr<T>::f(p[1]) + Tr<T>::r(v1);
     *reinterpret_cast<uint32_t*>(p) = Tr<T>::pack(a, b);
+  }
+  __device__ bool chunk32(int r, int c0, const float* v) const {
+    T* p = x + (size_t)r * ldx + c0;
+    if (!al16(p)) return false;
+    uint4 xv[4];
+    ld16x4(p, xv);
+    const T* xe = reinterpret_cast<const T*>(xv);
+    uint4 ov[4];
+    uint32_t* ow = reinterpret_cast<uint32_t*>(ov);
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      ow[j] = Tr<T>::pack(Tr<T>::f(xe[2 * j]) + Tr<T>::r(v[2 * j]),
+                          Tr<T>::f(xe[2 * j + 1]) + Tr<T>::r(v[2 * j + 1]));
+    st16x4(p, ov);
+    return true;
   }
 };
 
@@ -85,6 +145,27 @@ struct EpiGatedResid {  // suffix residual (gemma_dual.py:91-94): x = round(x + 
     *reinterpret_cast<uint32_t*>(p) = Tr<T>::pack(a, b);
     return make_float2(a, b);
   }
+  __device__ bool chunk32(int r, int c0, const float* v) const {
+    const T* g = gate + (size_t)(r / rows_per_gate) * gate_stride + c0;
+    T* p = x + (size_t)r * ldx + c0;
+    if (!al16(p) || !al16(g)) return false;
+    uint4 xv[4], gv[4];
+    ld16x4(p, xv);
+    ld16x4(g, gv);
+    const T* xe = reinterpret_cast<const T*>(xv);
+    const T* ge = reinterpret_cast<const T*>(gv);
+    uint4 ov[4];
+    uint32_t* ow = reinterpret_cast<uint32_t*>(ov);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const float a = Tr<T>::r(Tr<T>::f(xe[2 * j]) + Tr<T>::r(Tr<T>::r(v[2 * j]) * Tr<T>::f(ge[2 * j])));
+      const float b = Tr<T>::r(Tr<T>::f(xe[2 * j + 1]) +
+                               Tr<T>::r(Tr<T>::r(v[2 * j + 1]) * Tr<T>::f(ge[2 * j + 1])));
+      ow[j] = Tr<T>::pack(a, b);
+    }
+    st16x4(p, ov);
+    return true;
+  }
 };
 
 // GeGLU (gemma_dual.py:132-135) on interleaved gate/up weights: packed weight row 2j is gate
@@ -98,6 +179,21 @@ struct EpiGeglu {
   __device__ void operator()(int r, int c, float v0, float v1) const {
     float g = Tr<T>::r(gelu_tanh_f(Tr<T>::r(v0)));
     h[(size_t)r * ldh + (c >> 1)] = Tr<T>::t(g * Tr<T>::r(v1));
+  }
+  __device__ bool chunk32(int r, int c0, const float* v) const {
+    T* o = h + (size_t)r * ldh + (c0 >> 1);
+    if (!al16(o)) return false;
+    uint4 ov[2];
+    uint32_t* ow = reinterpret_cast<uint32_t*>(ov);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float g0 = Tr<T>::r(gelu_tanh_f(Tr<T>::r(v[4 * j])));
+      const float g1 = Tr<T>::r(gelu_tanh_f(Tr<T>::r(v[4 * j + 2])));
+      ow[j] = Tr<T>::pack(g0 * Tr<T>::r(v[4 * j + 1]), g1 * Tr<T>::r(v[4 * j + 3]));
+    }
+    reinterpret_cast<uint4*>(o)[0] = ov[0];
+    reinterpret_cast<uint4*>(o)[1] = ov[1];
+    return true;
   }
 };
 
@@ -158,6 +254,56 @@ struct EpiQkvRope {
       T* p = v + (((size_t)b * KV + head) * T_len + pos) * hd + d;
       *reinterpret_cast<uint32_t*>(p) = Tr<T>::pack(v0, v1);
     }
+  }
+  // 32 columns = 16 RoPE pairs (i0 .. i0+15) of one head, or 32 v dims of one head
+  __device__ bool chunk32(int r, int c_local0, const float* val) const {
+    if (hd < 32) return false;
+    const int c0 = c_local0 + col0;
+    const int hq = H * hd, hkv = KV * hd;
+    const int b = r / T_len, pos = r - b * T_len;
+    if (c0 < hq + hkv) {
+      const bool isq = c0 < hq;
+      const int cc = isq ? c0 : c0 - hq;
+      const int head = cc / hd, i0 = (cc - head * hd) >> 1, half = hd >> 1;
+      const size_t t = (size_t)b * cs_bstride + (size_t)pos * half + i0;
+      float* base = isq ? q + ((size_t)r * H + head) * hd
+                        : k + (((size_t)b * KV + head) * T_len + pos) * hd;
+      if (!al16(cos + t) || !al16(sin + t) || !al16(base + i0) || !al16(base + i0 + half))
+        return false;
+      float cs[16], sn[16];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        *reinterpret_cast<float4*>(cs + 4 * u) = reinterpret_cast<const float4*>(cos + t)[u];
+        *reinterpret_cast<float4*>(sn + 4 * u) = reinterpret_cast<const float4*>(sin + t)[u];
+      }
+      float o1[16], o2[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const float x1 = Tr<T>::r(val[2 * j]), x2 = Tr<T>::r(val[2 * j + 1]);
+        o1[j] = __fsub_rn(__fmul_rn(x1, cs[j]), __fmul_rn(x2, sn[j]));
+        o2[j] = __fadd_rn(__fmul_rn(x2, cs[j]), __fmul_rn(x1, sn[j]));
+        if (isq) {
+          o1[j] = __fmul_rn(o1[j], qscale);
+          o2[j] = __fmul_rn(o2[j], qscale);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        reinterpret_cast<float4*>(base + i0)[u] = *reinterpret_cast<const float4*>(o1 + 4 * u);
+        reinterpret_cast<float4*>(base + i0 + half)[u] = *reinterpret_cast<const float4*>(o2 + 4 * u);
+      }
+    } else {
+      const int cc = c0 - hq - hkv;
+      const int head = cc / hd, d = cc - head * hd;
+      T* p = v + (((size_t)b * KV + head) * T_len + pos) * hd + d;
+      if (!al16(p)) return false;
+      uint4 ov[4];
+      uint32_t* ow = reinterpret_cast<uint32_t*>(ov);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) ow[j] = Tr<T>::pack(val[2 * j], val[2 * j + 1]);
+      st16x4(p, ov);
+    }
+    return true;
   }
 };
 

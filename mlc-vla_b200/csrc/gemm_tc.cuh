@@ -277,15 +277,23 @@ __global__ void __launch_bounds__(192, 1)
       if (!ok) break;
       tc_fence_after();
       const int row = m0 + q * 32 + lane;
+      // one thread per accumulator row; each 32-column chunk goes through the functor's
+      // vectorised chunk32 (operands loaded before results are stored), the next chunk's
+      // operands are requested into L1 while this one is finished
+      if (row < M) epi.prefetch(row, n0);
 #pragma unroll 1
       for (int c = 0; c < BN; c += 32) {
         uint32_t v[32];
         tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + acc * BN + c, v);
         if (row < M) {
+          if (c + 32 < BN && n0 + c + 32 < N) epi.prefetch(row, n0 + c + 32);
+          const float* vf = reinterpret_cast<const float*>(v);
+          if (!(n0 + c + 32 <= N && epi.chunk32(row, n0 + c, vf))) {
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int col = n0 + c + 2 * j;
-            if (col < N) epi(row, col, __uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]));
+            for (int j = 0; j < 16; ++j) {
+              const int col = n0 + c + 2 * j;
+              if (col < N) epi(row, col, vf[2 * j], vf[2 * j + 1]);
+            }
           }
         }
       }
