@@ -1,0 +1,428 @@
+// Multi-query attention on 5th-generation tensor cores (fp16 models, one kv head), for both
+// halves of the M1 path (gemma_dual.py:97-122 `_sdpa`; prefill attn_prefill_e0 :236-253,
+// denoise attn_decode_e1 :255-275).
+//
+// A CTA owns 128 query rows (row j of batch b = token j / H, head j % H) and a range of 64-key
+// tiles; the key tiles of a row tile may be split over a cluster of CTAs, whose partials are
+// merged through distributed shared memory in rank order.
+//   * S = Q·Kᵀ: tcgen05.mma kind::f16, M=128, N=64, K=hd, fp32 accumulator in TMEM. q (post-RoPE,
+//     pre-scaled by hd^-0.5) and k (post-RoPE, stored at half scale so that no finite fp16-range
+//     value can overflow) are rounded to fp16 by the q/k/v epilogue: the same 10-bit mantissa as
+//     the tf32 inputs tensor cores take for fp32 operands, with round-to-nearest; the product is
+//     accumulated in fp32 and doubled exactly.
+//   * softmax: one thread per row reads its 64 logits from TMEM, adds the fp32 pad mask (0 / -1e9
+//     for prefix keys, 0 for suffix keys), and keeps a running max m and sum l in fp32. The
+//     probabilities exp(s − m) are rounded to fp16 (the V dtype) and written to shared memory as
+//     the A operand of the next MMA. O is rescaled only when the row max grows by more than
+//     e^8 (then O is read from TMEM, scaled and written back); until then probabilities are taken
+//     against the older, smaller max, at most e^8 ≈ 2981, well inside fp16.
+//   * O += P·V: tcgen05.mma kind::f16, M=128, N=hd, K=64, V read MN-major straight from its
+//     cache layout ([keys, hd], hd contiguous), fp32 accumulator in TMEM (hd columns).
+//   * final O / l (or, with key splits, the (m, l, O) partials merged across the cluster).
+// Warp roles: warp 0 TMA producer (Q once, K/V tiles through a 2-stage ring; cached prefix tiles
+// are requested before griddepcontrol.wait), warp 1 MMA issuer, warps 2-5 softmax/epilogue.
+// All waits are bounded (gemm_tc.cuh: mbar_wait).
+#pragma once
+
+#include "gemm_skinny.cuh"
+
+namespace pi0 {
+namespace atc {
+
+using namespace tc;
+using sk::cluster_rank;
+using sk::cluster_sync;
+using sk::ld_cluster4;
+using sk::map_rank;
+using sk::workers_sync;
+
+constexpr int KB = 64;             // keys per tile
+constexpr int NT = 192;
+constexpr float kRescale = 8.0f;   // rescale O when the row max grows by more than this
+
+template <int HD>
+struct AtcSmem {
+  static constexpr int NKB = HD / 64;               // 64-wide head-dim blocks
+  static constexpr int Q_BYTES = 128 * HD * 2;      // NKB boxes [64 hd × 128 rows]
+  static constexpr int K_BYTES = KB * HD * 2;       // NKB boxes [64 hd × 64 keys]
+  static constexpr int V_BYTES = KB * HD * 2;
+  static constexpr int STAGE = K_BYTES + V_BYTES;
+  static constexpr int P_OFF = Q_BYTES + 2 * STAGE;
+  static constexpr int P_BYTES = 128 * KB * 2;      // [128 rows × 64 keys] fp16
+  static constexpr int LOAD = P_OFF + P_BYTES;
+  static constexpr int OLD = HD + 4;                // merge buffer row stride (floats)
+  static constexpr int MERGE = 128 * OLD * 4 + 128 * 8;
+  static constexpr int BYTES = (LOAD > MERGE ? LOAD : MERGE) + 1024;
+};
+
+struct AtcArgs {
+  int rows;           // query rows per batch element: Tq·H
+  int LA, LB;         // keys of segment A (prefix cache) and B (suffix; 0 in prefill)
+  int ntA, nt;        // key tiles of A, all key tiles
+  int tps;            // key tiles per split
+  const float* maskA; // [B, LA] additive fp32, or null
+  void* out;          // [B·rows, HD] fp16
+  int* err;
+  int a_ready;        // segment A was written before the previous kernel
+  uint32_t v_lbo, v_sbo;  // MN-major V descriptor: byte stride between 64-dim blocks / 8-key groups
+};
+
+// Shared-memory matrix descriptor, MN-major operand in the 128-byte swizzle layout that TMA
+// writes for a [64 contiguous elements × rows] box.
+__device__ __forceinline__ uint64_t desc_sw128_mn(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
+      "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
+      "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+
+template <int HD>
+__global__ void __launch_bounds__(NT, 1)
+    attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKA,
+                   const __grid_constant__ CUtensorMap tmVA, const __grid_constant__ CUtensorMap tmKB,
+                   const __grid_constant__ CUtensorMap tmVB, AtcArgs a) {
+  using S = AtcSmem<HD>;
+  constexpr int NKB = S::NKB;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  __shared__ __align__(8) uint64_t q_full, kv_full[2], kv_empty[2], s_full, s_free, p_full,
+      pv_done, drain;
+  __shared__ uint32_t s_tmem;
+  __shared__ float s_mask[KB];
+  __shared__ float s_w[128][16];
+  __shared__ float s_inv[128];
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int b = blockIdx.z;
+  const int row0 = blockIdx.x * 128;
+  const int nsplit = gridDim.y;
+  const uint32_t rank = cluster_rank();
+  const int tbeg = blockIdx.y * a.tps;
+  const int n = max(0, min(a.nt, tbeg + a.tps) - tbeg);
+  uint8_t* sQ = base;
+  uint8_t* sP = base + S::P_OFF;
+  auto sK = [&](int s) { return base + S::Q_BYTES + s * S::STAGE; };
+  auto sV = [&](int s) { return base + S::Q_BYTES + s * S::STAGE + S::K_BYTES; };
+
+  if (tid == 0) {
+    mbar_init(&q_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    mbar_init(&s_full, 1);
+    mbar_init(&s_free, 4);
+    mbar_init(&p_full, 4);
+    mbar_init(&pv_done, 1);
+    mbar_init(&drain, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmKA);
+    tma_prefetch_desc(&tmVA);
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(&s_tmem)),
+                 "r"(512u));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s_tmem;  // S: columns [0, 64); O: columns [256, 256 + HD)
+
+  auto issue_kv = [&](int i) {
+    const int s = i & 1, tile = tbeg + i;
+    const bool inA = tile < a.ntA;
+    const CUtensorMap* mk = inA ? &tmKA : &tmKB;
+    const CUtensorMap* mv = inA ? &tmVA : &tmVB;
+    const int y = inA ? b * a.LA + tile * KB : b * a.LB + (tile - a.ntA) * KB;
+    mbar_expect_tx(&kv_full[s], S::STAGE);
+#pragma unroll
+    for (int kb = 0; kb < NKB; ++kb) {
+      tma_load_2d(sK(s) + kb * (KB * 128), mk, &kv_full[s], kb * 64, y);
+      tma_load_2d(sV(s) + kb * (KB * 128), mv, &kv_full[s], kb * 64, y);
+    }
+  };
+
+  // tiles of the cached prefix do not depend on the previous kernel
+  int issued = 0;
+  if (tid == 0 && a.a_ready)
+    while (issued < min(n, 2) && tbeg + issued < a.ntA) issue_kv(issued++);
+  pdl_trigger();
+  pdl_wait();
+
+  if (warp == 0) {
+    if (lane == 0) {  // producer
+      mbar_expect_tx(&q_full, S::Q_BYTES);
+#pragma unroll
+      for (int kb = 0; kb < NKB; ++kb)
+        tma_load_2d(sQ + kb * (128 * 128), &tmQ, &q_full, kb * 64, b * a.rows + row0);
+      for (int i = issued; i < n; ++i) {
+        if (i >= 2 && !mbar_wait(&kv_empty[i & 1], ((i >> 1) - 1) & 1, a.err, ERR_TIMEOUT_PRODUCER))
+          break;
+        issue_kv(i);
+        issued = i + 1;
+      }
+      // no copy into this CTA's shared memory may still be in flight when it exits
+      mbar_wait(&q_full, 0, a.err, ERR_TIMEOUT_PRODUCER, false);
+      for (int i = max(0, issued - 2); i < issued; ++i)
+        mbar_wait(&kv_full[i & 1], (i >> 1) & 1, a.err, ERR_TIMEOUT_PRODUCER, false);
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && n > 0) {  // MMA issuer
+      constexpr uint32_t id_s = idesc_f16<__half>(128, KB);
+      constexpr uint32_t id_o = idesc_f16<__half>(128, HD) | (1u << 16);  // B (V) MN-major
+      bool ok = mbar_wait(&q_full, 0, a.err, ERR_TIMEOUT_MMA);
+      auto qk = [&](int i) -> bool {
+        const int s = i & 1;
+        if (!mbar_wait(&kv_full[s], (i >> 1) & 1, a.err, ERR_TIMEOUT_MMA)) return false;
+        tc_fence_after();
+#pragma unroll
+        for (int kb = 0; kb < NKB; ++kb) {
+          const uint64_t da = desc_sw128(smem_u32(sQ + kb * (128 * 128)));
+          const uint64_t db = desc_sw128(smem_u32(sK(s) + kb * (KB * 128)));
+#pragma unroll
+          for (int k = 0; k < 4; ++k) umma_f16(tmem, da + 2 * k, db + 2 * k, id_s, (kb | k) != 0);
+        }
+        umma_commit(&s_full);
+        return true;
+      };
+      auto pv = [&](int i) -> bool {
+        const int s = i & 1;
+        if (!mbar_wait(&p_full, i & 1, a.err, ERR_TIMEOUT_MMA)) return false;
+        tc_fence_after();
+        const uint64_t da = desc_sw128(smem_u32(sP));
+        const uint64_t db = desc_sw128_mn(smem_u32(sV(s)), a.v_lbo, a.v_sbo);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)  // 16 keys (2048 bytes of V rows) per step
+          umma_f16(tmem + 256, da + 2 * k, db + (uint64_t)(128 * k), id_o, (i | k) != 0);
+        umma_commit(&kv_empty[s]);
+        umma_commit(&pv_done);
+        return true;
+      };
+      ok = ok && qk(0);
+      for (int i = 0; i < n && ok; ++i) {
+        if (i + 1 < n) ok = mbar_wait(&s_free, i & 1, a.err, ERR_TIMEOUT_MMA) && qk(i + 1);
+        ok = ok && pv(i);
+      }
+      // every issued MMA completes before TMEM is released
+      umma_commit(&drain);
+      mbar_wait(&drain, 0, a.err, ERR_TIMEOUT_MMA, false);
+    }
+  } else {  // warps 2-5: softmax, one thread per query row
+    const int q4 = warp & 3, r = q4 * 32 + lane, wt = tid - 64;
+    const uint32_t tS = tmem + ((uint32_t)(q4 * 32) << 16);
+    const uint32_t tO = tS + 256;
+    float m_ref = -1e30f, l = 0.f;
+    auto mask_of = [&](int tile) -> float {
+      if (tile < a.ntA) {
+        const int key = tile * KB + wt;
+        return key < a.LA ? (a.maskA ? a.maskA[(size_t)b * a.LA + key] : 0.f) : -1e30f;
+      }
+      const int key = (tile - a.ntA) * KB + wt;
+      return key < a.LB ? 0.f : -1e30f;
+    };
+    float mnext = (wt < KB && n > 0) ? mask_of(tbeg) : 0.f;
+    // after a failed (timed-out) wait the loop keeps running without work, so the four warps
+    // always meet at the same named barriers
+    bool ok = true;
+    for (int i = 0; i < n; ++i) {
+      workers_sync();  // everyone is done with the previous tile's mask
+      if (wt < KB) s_mask[wt] = mnext;
+      workers_sync();
+      if (wt < KB && i + 1 < n) mnext = mask_of(tbeg + i + 1);
+      if (ok) ok = mbar_wait(&s_full, i & 1, a.err, ERR_TIMEOUT_EPI);
+      ok = !__any_sync(0xffffffffu, !ok);
+      uint32_t s0[32], s1[32];
+      if (ok) {
+        tc_fence_after();
+        tmem_ld32(tS, s0);
+        tmem_ld32(tS + 32, s1);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s_free);
+      }
+      if (!ok) continue;
+      float sv[KB];
+      float mt = -1e30f;
+#pragma unroll
+      for (int j = 0; j < KB; ++j) {
+        const float raw = __uint_as_float(j < 32 ? s0[j] : s1[j - 32]);
+        sv[j] = __fadd_rn(2.f * raw, s_mask[j]);
+        mt = fmaxf(mt, sv[j]);
+      }
+      if (i == 0) {
+        m_ref = mt;
+      } else {
+        // O and the P buffer are free once the previous P·V has finished
+        ok = mbar_wait(&pv_done, (i - 1) & 1, a.err, ERR_TIMEOUT_EPI);
+        ok = !__any_sync(0xffffffffu, !ok);
+        if (!ok) continue;
+        tc_fence_after();
+        const bool need = mt > m_ref + kRescale;
+        if (__any_sync(0xffffffffu, need)) {
+          const float alpha = need ? expf(m_ref - mt) : 1.f;
+#pragma unroll 1
+          for (int c = 0; c < HD; c += 32) {
+            uint32_t ov[32];
+            tmem_ld32(tO + c, ov);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) ov[j] = __float_as_uint(__uint_as_float(ov[j]) * alpha);
+            tmem_st32(tO + c, ov);
+          }
+          asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+          if (need) {
+            l *= alpha;
+            m_ref = mt;
+          }
+        }
+      }
+      // probabilities against m_ref, rounded to fp16, into the swizzled A operand
+      float rs = 0.f;
+#pragma unroll
+      for (int c = 0; c < KB / 8; ++c) {
+        uint32_t w4[4];
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          const float p0 = expf(sv[8 * c + 2 * h] - m_ref);
+          const float p1 = expf(sv[8 * c + 2 * h + 1] - m_ref);
+          rs += p0 + p1;
+          w4[h] = Tr<__half>::pack(p0, p1);
+        }
+        *reinterpret_cast<uint4*>(sP + r * 128 + ((c ^ (r & 7)) << 4)) =
+            make_uint4(w4[0], w4[1], w4[2], w4[3]);
+      }
+      l += rs;
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full);
+    }
+    if (ok && n > 0) {
+      ok = mbar_wait(&pv_done, (n - 1) & 1, a.err, ERR_TIMEOUT_EPI, false);
+      tc_fence_after();
+    }
+    const bool have = __all_sync(0xffffffffu, ok) && n > 0;
+    if (nsplit == 1) {
+      const int j = row0 + r;
+      __half* out = reinterpret_cast<__half*>(a.out) + ((size_t)b * a.rows + j) * HD;
+      const float inv = have && l > 0.f ? 1.f / l : 0.f;
+#pragma unroll 1
+      for (int c = 0; c < HD; c += 32) {
+        uint32_t ov[32];
+        if (have) tmem_ld32(tO + c, ov);
+        uint4 pk[4];
+        uint32_t* pw = reinterpret_cast<uint32_t*>(pk);
+#pragma unroll
+        for (int h = 0; h < 16; ++h)
+          pw[h] = have ? Tr<__half>::pack(__uint_as_float(ov[2 * h]) * inv,
+                                          __uint_as_float(ov[2 * h + 1]) * inv)
+                       : 0u;
+        if (j < a.rows)
+#pragma unroll
+          for (int u = 0; u < 4; ++u) reinterpret_cast<uint4*>(out + c)[u] = pk[u];
+      }
+    } else {
+      // partial (m, l, unnormalised O) of this split into shared memory for the merge
+      float* sO = reinterpret_cast<float*>(base);
+      float* sML = sO + 128 * S::OLD;
+#pragma unroll 1
+      for (int c = 0; c < HD; c += 32) {
+        uint32_t ov[32];
+        if (have) tmem_ld32(tO + c, ov);
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          *reinterpret_cast<float4*>(sO + r * S::OLD + c + 4 * u) =
+              have ? make_float4(__uint_as_float(ov[4 * u]), __uint_as_float(ov[4 * u + 1]),
+                                 __uint_as_float(ov[4 * u + 2]), __uint_as_float(ov[4 * u + 3]))
+                   : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+      sML[2 * r] = have ? m_ref : -1e30f;
+      sML[2 * r + 1] = have ? l : 0.f;
+    }
+  }
+
+  if (nsplit > 1) {
+    // ---- merge the key splits of this row tile: rank r finishes rows [r·rpr, (r+1)·rpr) ----
+    tc_fence_before();
+    cluster_sync();
+    const float* sO = reinterpret_cast<const float*>(base);
+    const float* sML = sO + 128 * S::OLD;
+    const uint32_t oaddr = smem_u32(sO), maddr = smem_u32(sML);
+    const int rpr = (128 + nsplit - 1) / nsplit;
+    const int rbeg = rank * rpr, rend = min(128, rbeg + rpr);
+    for (int rr = tid; rr < rend - rbeg; rr += NT) {
+      const int row = rbeg + rr;
+      float mm[16], ll[16];
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        mm[c] = -1e30f;
+        ll[c] = 0.f;
+        if (c < nsplit) {
+          const float4 v = ld_cluster4(map_rank(maddr + (row & ~1) * 8, c));
+          mm[c] = (row & 1) ? v.z : v.x;
+          ll[c] = (row & 1) ? v.w : v.y;
+        }
+      }
+      float M = -1e30f;
+#pragma unroll
+      for (int c = 0; c < 16; ++c) M = fmaxf(M, mm[c]);
+      float L = 0.f;
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        const float w = c < nsplit ? expf(mm[c] - M) : 0.f;
+        s_w[rr][c] = w;
+        L += w * ll[c];
+      }
+      s_inv[rr] = L > 0.f ? 1.f / L : 0.f;
+    }
+    __syncthreads();
+    const int items = (rend - rbeg) * (HD / 4);
+    for (int it = tid; it < items; it += NT) {
+      const int rr = it / (HD / 4), d = (it % (HD / 4)) * 4;
+      const int row = rbeg + rr, j = row0 + row;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int c = 0; c < nsplit; ++c) {
+        const float4 v = ld_cluster4(map_rank(oaddr + (row * S::OLD + d) * 4, c));
+        const float w = s_w[rr][c];
+        acc.x += w * v.x;
+        acc.y += w * v.y;
+        acc.z += w * v.z;
+        acc.w += w * v.w;
+      }
+      if (j < a.rows) {
+        const float inv = s_inv[rr];
+        __half* out = reinterpret_cast<__half*>(a.out) + ((size_t)b * a.rows + j) * HD + d;
+        *reinterpret_cast<uint2*>(out) =
+            make_uint2(Tr<__half>::pack(acc.x * inv, acc.y * inv), Tr<__half>::pack(acc.z * inv, acc.w * inv));
+      }
+    }
+    cluster_sync();  // peers may still read this CTA's partial
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512u));
+  }
+}
+
+}  // namespace atc
+}  // namespace pi0

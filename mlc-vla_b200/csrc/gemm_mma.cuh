@@ -216,6 +216,10 @@ struct EpiQkvRope {
   int H, KV, hd;
   int col0;      // global column offset of this launch (skip q rows for the last prefill layer)
   float qscale;
+  // tensor-core attention operands (optional): q in the model dtype instead of fp32 q, and a
+  // model-dtype copy of k at half scale next to the fp32 cache entry
+  T* q16 = nullptr;
+  T* k16 = nullptr;
   __device__ void prefetch(int r, int c_local) const {
     const int c = c_local + col0;
     if (c < (H + KV) * hd) {
@@ -240,13 +244,22 @@ struct EpiQkvRope {
       float o1 = __fsub_rn(__fmul_rn(x1, cs), __fmul_rn(x2, sn));
       float o2 = __fadd_rn(__fmul_rn(x2, cs), __fmul_rn(x1, sn));
       if (isq) {
-        float* p = q + ((size_t)r * H + head) * hd;
-        p[i] = __fmul_rn(o1, qscale);
-        p[i + half] = __fmul_rn(o2, qscale);
+        const size_t qo = ((size_t)r * H + head) * hd;
+        if (q16) {
+          q16[qo + i] = Tr<T>::t(__fmul_rn(o1, qscale));
+          q16[qo + i + half] = Tr<T>::t(__fmul_rn(o2, qscale));
+        } else {
+          q[qo + i] = __fmul_rn(o1, qscale);
+          q[qo + i + half] = __fmul_rn(o2, qscale);
+        }
       } else {
-        float* p = k + (((size_t)b * KV + head) * T_len + pos) * hd;
-        p[i] = o1;
-        p[i + half] = o2;
+        const size_t ko = (((size_t)b * KV + head) * T_len + pos) * hd;
+        k[ko + i] = o1;
+        k[ko + i + half] = o2;
+        if (k16) {
+          k16[ko + i] = Tr<T>::t(0.5f * o1);
+          k16[ko + i + half] = Tr<T>::t(0.5f * o2);
+        }
       }
     } else {
       int cc = c - hq - hkv;
@@ -266,10 +279,15 @@ struct EpiQkvRope {
       const int cc = isq ? c0 : c0 - hq;
       const int head = cc / hd, i0 = (cc - head * hd) >> 1, half = hd >> 1;
       const size_t t = (size_t)b * cs_bstride + (size_t)pos * half + i0;
-      float* base = isq ? q + ((size_t)r * H + head) * hd
-                        : k + (((size_t)b * KV + head) * T_len + pos) * hd;
-      if (!al16(cos + t) || !al16(sin + t) || !al16(base + i0) || !al16(base + i0 + half))
-        return false;
+      const size_t off = isq ? ((size_t)r * H + head) * hd
+                             : (((size_t)b * KV + head) * T_len + pos) * hd;
+      float* base = isq ? q + off : k + off;
+      T* base16 = isq ? q16 : k16;
+      if (!al16(cos + t) || !al16(sin + t)) return false;
+      if (base16) {
+        if (!al16(base16 + off + i0) || !al16(base16 + off + i0 + half)) return false;
+      }
+      if ((!isq || !q16) && (!al16(base + i0) || !al16(base + i0 + half))) return false;
       float cs[16], sn[16];
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
@@ -287,10 +305,27 @@ struct EpiQkvRope {
           o2[j] = __fmul_rn(o2[j], qscale);
         }
       }
+      if (!isq || !q16) {
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        reinterpret_cast<float4*>(base + i0)[u] = *reinterpret_cast<const float4*>(o1 + 4 * u);
-        reinterpret_cast<float4*>(base + i0 + half)[u] = *reinterpret_cast<const float4*>(o2 + 4 * u);
+        for (int u = 0; u < 4; ++u) {
+          reinterpret_cast<float4*>(base + i0)[u] = *reinterpret_cast<const float4*>(o1 + 4 * u);
+          reinterpret_cast<float4*>(base + i0 + half)[u] = *reinterpret_cast<const float4*>(o2 + 4 * u);
+        }
+      }
+      if (base16) {
+        const float sc = isq ? 1.f : 0.5f;  // k at half scale
+        uint4 h1[2], h2[2];
+        uint32_t* w1 = reinterpret_cast<uint32_t*>(h1);
+        uint32_t* w2 = reinterpret_cast<uint32_t*>(h2);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          w1[j] = Tr<T>::pack(sc * o1[2 * j], sc * o1[2 * j + 1]);
+          w2[j] = Tr<T>::pack(sc * o2[2 * j], sc * o2[2 * j + 1]);
+        }
+        reinterpret_cast<uint4*>(base16 + off + i0)[0] = h1[0];
+        reinterpret_cast<uint4*>(base16 + off + i0)[1] = h1[1];
+        reinterpret_cast<uint4*>(base16 + off + i0 + half)[0] = h2[0];
+        reinterpret_cast<uint4*>(base16 + off + i0 + half)[1] = h2[1];
       }
     } else {
       const int cc = c0 - hq - hkv;

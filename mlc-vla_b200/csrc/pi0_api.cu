@@ -25,6 +25,7 @@
 
 #include "pi0b200.h"
 #include "attention.cuh"
+#include "attention_tc.cuh"
 #include "common.cuh"
 #include "gemm_mma.cuh"
 #include "gemm_tc.cuh"
@@ -105,6 +106,10 @@ struct pi0_ctx {
   float* qp = nullptr;
   void *xs = nullptr, *xsn = nullptr, *attn_s = nullptr, *hs = nullptr, *vsuf = nullptr;
   float *qs = nullptr, *ksuf = nullptr;
+  // tensor-core attention (fp16 models, one kv head): model-dtype q, and k copies at half scale
+  bool attn_tc = false;
+  void *q16p = nullptr, *q16s = nullptr, *kpre16 = nullptr, *ksuf16 = nullptr;
+  bool pdl_barrier = false;  // the next launch waits for full completion of the previous one
   void *t1 = nullptr, *cond = nullptr, *mods = nullptr;
   float* splitk_ws = nullptr;
   size_t splitk_floats = 0;
@@ -136,14 +141,14 @@ namespace {
 enum Fam {
   F_PRE_NORM, F_PRE_QKV, F_PRE_ATTN, F_PRE_O, F_PRE_GU, F_PRE_DOWN,
   F_DEN_TIME_MODS, F_DEN_ACT_IN, F_DEN_NORM, F_DEN_QKV, F_DEN_ATTN, F_DEN_O, F_DEN_GU,
-  F_DEN_DOWN, F_DEN_ACT_OUT, F_NUM
+  F_DEN_DOWN, F_DEN_ACT_OUT, F_DEN_KEYS16, F_NUM
 };
 const char* kFamName[F_NUM] = {
   "prefill.rmsnorm", "prefill.qkv_rope_gemm", "prefill.attention", "prefill.o_gemm",
   "prefill.gate_up_geglu_gemm", "prefill.down_gemm",
   "denoise.time_mlp_modulation_gemm", "denoise.action_in", "denoise.ada_rmsnorm",
   "denoise.qkv_rope_gemm", "denoise.attention", "denoise.o_gemm", "denoise.gate_up_geglu_gemm",
-  "denoise.down_gemm", "denoise.action_out_euler"};
+  "denoise.down_gemm", "denoise.action_out_euler", "denoise.prefix_keys_fp16"};
 
 int fail(pi0_ctx* c, int code, const std::string& msg) {
   if (c) c->err = msg;
@@ -214,7 +219,9 @@ int launch(pi0_ctx* ctx, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t s
   cfg.stream = st;
   cudaLaunchAttribute at[2];
   int n = 0;
-  if (ctx->pdl) {
+  const bool pdl = ctx->pdl && !ctx->pdl_barrier;
+  ctx->pdl_barrier = false;
+  if (pdl) {
     at[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     at[n].val.programmaticStreamSerializationAllowed = 1;
     ++n;
@@ -588,6 +595,72 @@ int time_and_mods(pi0_ctx* ctx, const T* te, int nsteps, cudaStream_t st) {
   return 0;
 }
 
+// Tensor-core attention (attention_tc.cuh) of `rows` = Tq·H query rows per request over key
+// segment A (kA16 / vA, LA keys) and segment B (kB16 / vB, LB keys, may be 0). Key splits: as
+// many as keep the grid within one wave (at most 16, one cluster), with every split at least
+// one 64-key tile.
+template <int HD>
+int attn_tc_launch_hd(pi0_ctx* ctx, int B, const __half* q16, int rows, const __half* kA16,
+                      const __half* vA, int LA, const __half* kB16, const __half* vB, int LB,
+                      const float* mask, __half* out, int a_ready, cudaStream_t st, int fam) {
+  CUtensorMap tq, tka, tva, tkb, tvb;
+  TRY(make_tmap(ctx, &tq, q16, B * rows, HD, HD, 128, false));
+  TRY(make_tmap(ctx, &tka, kA16, B * LA, HD, HD, atc::KB, false));
+  TRY(make_tmap(ctx, &tva, vA, B * LA, HD, HD, atc::KB, false));
+  if (LB > 0) {
+    TRY(make_tmap(ctx, &tkb, kB16, B * LB, HD, HD, atc::KB, false));
+    TRY(make_tmap(ctx, &tvb, vB, B * LB, HD, HD, atc::KB, false));
+  } else {
+    tkb = tka;
+    tvb = tva;
+  }
+  atc::AtcArgs a{};
+  a.rows = rows;
+  a.LA = LA;
+  a.LB = LB;
+  a.ntA = (LA + atc::KB - 1) / atc::KB;
+  a.nt = a.ntA + (LB + atc::KB - 1) / atc::KB;
+  const int row_tiles = (rows + 127) / 128;
+  int splits = std::max(1, std::min(16, ctx->num_sms / std::max(1, row_tiles * B)));
+  splits = std::min(splits, a.nt);
+  a.tps = (a.nt + splits - 1) / splits;
+  splits = (a.nt + a.tps - 1) / a.tps;
+  a.maskA = mask;
+  a.out = out;
+  a.err = ctx->dev_err;
+  a.a_ready = a_ready;
+  a.v_lbo = atc::KB * 128;  // next 64-dim block of a V tile
+  a.v_sbo = 1024;           // next 8 keys
+  Prof pr(ctx, fam, st);
+  return launch(ctx, atc::attn_tc_kernel<HD>, dim3(row_tiles, splits, B), dim3(atc::NT),
+                atc::AtcSmem<HD>::BYTES, st, dim3(1, splits, 1), tq, tka, tva, tkb, tvb, a);
+}
+
+int attn_tc_launch(pi0_ctx* ctx, int B, const __half* q16, int rows, const __half* kA16,
+                   const __half* vA, int LA, const __half* kB16, const __half* vB, int LB,
+                   const float* mask, __half* out, int a_ready, cudaStream_t st, int fam) {
+  switch (ctx->cfg.head_dim) {
+    case 64: return attn_tc_launch_hd<64>(ctx, B, q16, rows, kA16, vA, LA, kB16, vB, LB, mask, out, a_ready, st, fam);
+    case 128: return attn_tc_launch_hd<128>(ctx, B, q16, rows, kA16, vA, LA, kB16, vB, LB, mask, out, a_ready, st, fam);
+    case 256: return attn_tc_launch_hd<256>(ctx, B, q16, rows, kA16, vA, LA, kB16, vB, LB, mask, out, a_ready, st, fam);
+  }
+  return fail(ctx, PI0_ERR_UNSUPPORTED, "tensor-core attention: head_dim must be 64, 128 or 256");
+}
+
+// K cache (fp32, caller's layout) -> model-dtype copy at half scale for the tensor-core
+// attention; the next launch waits for it to complete (no programmatic overlap), so the cached
+// tiles the attention requests before its own dependency wait are already converted.
+int convert_prefix_keys(pi0_ctx* ctx, int B, const float* keys, cudaStream_t st) {
+  const pi0_config& g = ctx->cfg;
+  const size_t n = (size_t)g.depth * B * g.num_kv_heads * g.prefix_len * g.head_dim;
+  const size_t n4 = n / 4;
+  Prof pr(ctx, F_DEN_KEYS16, st);
+  TRY(launch(ctx, keys_half_scale_kernel<__half>, dim3((unsigned)((n4 + 255) / 256)), dim3(256), 0,
+             st, dim3(1, 1, 1), reinterpret_cast<const float4*>(keys), (__half*)ctx->kpre16, n4));
+  ctx->pdl_barrier = true;
+  return 0;
+}
+
 // ---- prefill ---------------------------------------------------------------------------------
 template <typename T>
 int run_prefill(pi0_ctx* ctx, int B, const T* prefix, const float* mask, float* keys, T* values,
@@ -609,6 +682,11 @@ int run_prefill(pi0_ctx* ctx, int B, const T* prefix, const float* mask, float* 
     TRY(rmsnorm<T>(ctx, x, xn, M, W0, (const T*)w.ln_in, nullptr, 1, 0, st, F_PRE_NORM));
     EpiQkvRope<T> eq{ctx->qp, kl, vl, ctx->rope_cos, ctx->rope_sin, 0, P, H, KV, hd, 0,
                      (float)std::pow((double)hd, -0.5)};
+    T* k16 = ctx->attn_tc ? (T*)ctx->kpre16 + l * kv_layer : nullptr;
+    if (ctx->attn_tc) {
+      eq.q16 = (T*)ctx->q16p;
+      eq.k16 = k16;
+    }
     const bool last = l == g.depth - 1;
     if (last) {  // only k and v of the last layer are ever read
       eq.col0 = hq;
@@ -617,6 +695,19 @@ int run_prefill(pi0_ctx* ctx, int B, const T* prefix, const float* mask, float* 
       break;
     }
     TRY(gemm<T>(ctx, xn, W0, (const T*)w.qkv, W0, M, hq + 2 * hkv, W0, eq, st, F_PRE_QKV));
+    if constexpr (!Tr<T>::kBf16) {
+      if (ctx->attn_tc) {
+        TRY(attn_tc_launch(ctx, B, (const __half*)ctx->q16p, P * H, (const __half*)k16,
+                           (const __half*)vl, P, nullptr, nullptr, 0, mask, (__half*)attn, 0, st,
+                           F_PRE_ATTN));
+        TRY(gemm<T>(ctx, attn, hq, (const T*)w.o, hq, M, W0, hq, EpiResid<T>{x, W0}, st, F_PRE_O));
+        TRY(rmsnorm<T>(ctx, x, xn, M, W0, (const T*)w.ln_post, nullptr, 1, 0, st, F_PRE_NORM));
+        TRY(gemm<T>(ctx, xn, W0, (const T*)w.gu, W0, M, 2 * F0, W0, EpiGeglu<T>{h, F0}, st,
+                    F_PRE_GU));
+        TRY(gemm<T>(ctx, h, F0, (const T*)w.d, F0, M, W0, F0, EpiResid<T>{x, W0}, st, F_PRE_DOWN));
+        continue;
+      }
+    }
     AttnArgs<T> a{};
     a.q = ctx->qp;
     a.kA = kl;
@@ -674,8 +765,23 @@ int run_suffix(pi0_ctx* ctx, int B, const float* keys, const T* values, const vo
     const T* m_post = mods + (size_t)(2 * l + 1) * mstride;
     EpiQkvRope<T> eq{ctx->qs, ctx->ksuf, (T*)ctx->vsuf, scos, ssin, S * (hd / 2), S, H, KV, hd, 0,
                      (float)std::pow((double)hd, -0.5)};
+    if (ctx->attn_tc) {
+      eq.q16 = (T*)ctx->q16s;
+      eq.k16 = (T*)ctx->ksuf16;
+    }
     TRY((gemm_w<T, true, false>(ctx, x, W1, (const T*)w.qkv, (const T*)w.qkv_p, M, hq + 2 * hkv,
                                 W1, eq, st, F_DEN_QKV, m_in, xn)));
+    bool done_attn = false;
+    if constexpr (!Tr<T>::kBf16) {
+      if (ctx->attn_tc) {
+        TRY(attn_tc_launch(ctx, B, (const __half*)ctx->q16s, S * H,
+                           (const __half*)ctx->kpre16 + l * kv_layer, (const __half*)values + l * kv_layer,
+                           P, (const __half*)ctx->ksuf16, (const __half*)ctx->vsuf, S, mask,
+                           (__half*)attn, 1, st, F_DEN_ATTN));
+        done_attn = true;
+      }
+    }
+    if (!done_attn) {
     AttnArgs<T> a{};
     a.q = ctx->qs;
     a.kA = keys + l * kv_layer;
@@ -691,6 +797,7 @@ int run_suffix(pi0_ctx* ctx, int B, const float* keys, const T* values, const vo
     a.out = attn;
     a.a_is_ready = 1;  // the prefix K/V cache comes from prefill, not from this step
     TRY(attn_launch<T>(ctx, a, B, true, st, F_DEN_ATTN));
+    }
     TRY((gemm_w<T, false, true>(ctx, attn, hq, (const T*)w.o, (const T*)w.o_p, M, W1, hq,
                                 EpiGatedResid<T>{x, W1, m_in + 2 * W1, M, 0}, st, F_DEN_O)));
     TRY((gemm_w<T, true, false>(ctx, x, W1, (const T*)w.gu, (const T*)w.gu_p, M, 2 * F1, W1,
@@ -713,6 +820,7 @@ template <typename T>
 int run_step(pi0_ctx* ctx, int B, const float* keys, const T* values, const T* x_t, const T* te,
              const float* scos, const float* ssin, const float* mask, float* v_out,
              cudaStream_t st) {
+  if (ctx->attn_tc) TRY(convert_prefix_keys(ctx, B, keys, st));
   TRY(time_and_mods<T>(ctx, te, 1, st));
   return run_suffix<T>(ctx, B, keys, values, x_t, false, (const T*)ctx->mods, scos, ssin, mask,
                        v_out, 0, 0.f, st);
@@ -728,6 +836,7 @@ int run_loop_body(pi0_ctx* ctx, int B, const float* keys, const T* values, const
   if (x_out != x0)
     CK(cudaMemcpyAsync(x_out, x0, (size_t)B * g.action_horizon * g.action_dim * sizeof(float),
                        cudaMemcpyDeviceToDevice, st));
+  if (ctx->attn_tc) TRY(convert_prefix_keys(ctx, B, keys, st));
   TRY(time_and_mods<T>(ctx, tes, N, st));
   const float dt = (float)(-1.0 / N);
   for (int i = 0; i < N; ++i)
@@ -777,8 +886,22 @@ int attr_attn(pi0_ctx* ctx) {
                           1));
   return 0;
 }
+template <int HD>
+int attr_attn_tc(pi0_ctx* ctx) {
+  CK(cudaFuncSetAttribute(atc::attn_tc_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                          atc::AtcSmem<HD>::BYTES));
+  CK(cudaFuncSetAttribute(atc::attn_tc_kernel<HD>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+  return 0;
+}
 template <typename T>
 int setup_attrs(pi0_ctx* ctx) {
+  if (ctx->attn_tc) {
+    switch (ctx->cfg.head_dim) {
+      case 64: TRY(attr_attn_tc<64>(ctx)); break;
+      case 128: TRY(attr_attn_tc<128>(ctx)); break;
+      case 256: TRY(attr_attn_tc<256>(ctx)); break;
+    }
+  }
   TRY(attr_gemm_both<T, EpiQkvRope<T>>(ctx));
   TRY(attr_gemm_both<T, EpiResid<T>>(ctx));
   TRY(attr_gemm_both<T, EpiGatedResid<T>>(ctx));
@@ -945,6 +1068,13 @@ int alloc_all(pi0_ctx* ctx) {
   TRY(dev_alloc(ctx, (void**)&ctx->qs, MS * hq * 4));
   TRY(dev_alloc(ctx, (void**)&ctx->ksuf, B * hkv * S * 4));
   TRY(dev_alloc(ctx, &ctx->vsuf, B * hkv * S * e));
+  ctx->attn_tc = e == 2 && g.dtype == PI0_F16 && KV == 1 && hd % 64 == 0 && hd <= 256;
+  if (ctx->attn_tc) {
+    TRY(dev_alloc(ctx, &ctx->q16p, MP * hq * e));
+    TRY(dev_alloc(ctx, &ctx->q16s, MS * hq * e));
+    TRY(dev_alloc(ctx, &ctx->kpre16, (size_t)g.depth * B * hkv * P * e));
+    TRY(dev_alloc(ctx, &ctx->ksuf16, B * hkv * S * e));
+  }
   TRY(dev_alloc(ctx, &ctx->t1, (size_t)N * W1 * e));
   TRY(dev_alloc(ctx, &ctx->cond, (size_t)N * W1 * e));
   TRY(dev_alloc(ctx, &ctx->mods, (size_t)N * nmodw * e));

@@ -258,4 +258,17 @@ __global__ void div_check_kernel(const float* __restrict__ a, const float* __res
   if (i < n) out[i] = div_by_rcp(a[i], b[i], __frcp_rn(b[i]));
 }
 
+// Model-dtype copy of an fp32 K cache at half scale, the operand of the tensor-core attention
+// (attention_tc.cuh): k16[i] = RN(0.5·k[i]). n4 = elements / 4.
+template <typename T>
+__global__ void keys_half_scale_kernel(const float4* __restrict__ k, T* __restrict__ k16, size_t n4) {
+  const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n4) return;
+  const float4 v = k[i];
+  uint2 o;
+  o.x = Tr<T>::pack(0.5f * v.x, 0.5f * v.y);
+  o.y = Tr<T>::pack(0.5f * v.z, 0.5f * v.w);
+  reinterpret_cast<uint2*>(k16)[i] = o;
+}
+
 }  // namespace pi0
