@@ -394,19 +394,28 @@ __global__ void __launch_bounds__(NT, 1)
       s_inv[rr] = L > 0.f ? 1.f / L : 0.f;
     }
     __syncthreads();
+    // one (row, 4 dims) item per thread and pass; the nsplit partials of an item are loaded
+    // together (static indices, predicated), then summed in rank order
     const int items = (rend - rbeg) * (HD / 4);
+#pragma unroll 1
     for (int it = tid; it < items; it += NT) {
       const int rr = it / (HD / 4), d = (it % (HD / 4)) * 4;
       const int row = rbeg + rr, j = row0 + row;
+      const uint32_t off = oaddr + (row * S::OLD + d) * 4;
+      float4 v[16];
+#pragma unroll
+      for (int c = 0; c < 16; ++c)
+        if (c < nsplit) v[c] = ld_cluster4(map_rank(off, c));
       float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int c = 0; c < nsplit; ++c) {
-        const float4 v = ld_cluster4(map_rank(oaddr + (row * S::OLD + d) * 4, c));
-        const float w = s_w[rr][c];
-        acc.x += w * v.x;
-        acc.y += w * v.y;
-        acc.z += w * v.z;
-        acc.w += w * v.w;
-      }
+#pragma unroll
+      for (int c = 0; c < 16; ++c)
+        if (c < nsplit) {
+          const float w = s_w[rr][c];
+          acc.x += w * v[c].x;
+          acc.y += w * v[c].y;
+          acc.z += w * v[c].z;
+          acc.w += w * v[c].w;
+        }
       if (j < a.rows) {
         const float inv = s_inv[rr];
         __half* out = reinterpret_cast<__half*>(a.out) + ((size_t)b * a.rows + j) * HD + d;
