@@ -93,6 +93,20 @@ def work_model(cfg, batch):
     return w
 
 
+# DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) from one ncu capture of each
+# kernel at the bench's configuration, reported as the roofline's "traffic" when that family is the
+# dominant one; traffic near the algorithmic bytes means no operand is read twice.
+NCU_TRAFFIC = {
+    "denoise.gate_up_geglu_gemm": 16936704,
+    "denoise.qkv_rope_gemm": 5465344,
+    "denoise.o_gemm": 4541440,
+    "denoise.down_gemm": 8940544,
+    "denoise.attention": 1315584,
+    "prefill.gate_up_geglu_gemm": 138220032 + 17278720,
+    "prefill.attention": 5023232,
+}
+
+
 # ------------------------------------------------------------------------------------------
 # clocks sampled during the timed region
 # ------------------------------------------------------------------------------------------
@@ -112,7 +126,7 @@ class ClockSampler:
             self.f = open(self.path, "w")
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+                 "-lms", "50"], stdout=self.f, stderr=subprocess.DEVNULL)
         except (OSError, FileNotFoundError):
             self.proc = None
         return self
@@ -394,7 +408,8 @@ def run_b200(args):
                 ent["gbs"] = round(wk[0] / (tot / 1e3) / 1e9, 1)
         families[k] = ent
     roofline = {"bound": bound, "kernel": dom, "achieved": round(achieved, 2), "peak": peak,
-                "unit": runit, "frac": round(achieved / peak, 4), "traffic": None,
+                "unit": runit, "frac": round(achieved / peak, 4),
+                "traffic": NCU_TRAFFIC.get(dom), "traffic_unit": "bytes per launch (ncu)",
                 "peak_source": f"{pk_kind} ({'bf16_tflops_sustained' if bound == 'tensor' else 'hbm_gbs'})",
                 "work_per_launch": work / max(1, fam[dom][0]), "families": families}
 
@@ -426,16 +441,73 @@ def run_b200(args):
     return 0
 
 
+def run_part(args):
+    """``--part prefill`` / ``--part step``: time one half of the chunk on one GPU (the prefill
+    alone, or one ``denoise_step_kv`` on a seeded random K/V cache), for per-kernel profiling.
+    Prints a JSON line with the part's mean ms; the chunk metric is the default mode."""
+    import torch
+
+    from mlc_vla.runtime import Pi0Runtime
+    from mlc_vla.sample import make_prefix_mask_np, make_rope_np, make_time_embs
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    cfg = full_config()
+    rt = Pi0Runtime(cfg, device=0)
+    rt.bind(make_weights(rt.named_params, dev, seed=0))
+    P, S, D, W0 = cfg.prefix_len, cfg.suffix_len, cfg.action_dim, cfg.vlm.width
+    g = torch.Generator(device=dev).manual_seed(1)
+    pm = torch.from_numpy(make_prefix_mask_np(P)).to(dev)
+    vlm = cfg.vlm
+    kv = (vlm.depth, 1, vlm.num_kv_heads, P, vlm.head_dim)
+    if args.part == "prefill":
+        prefix = torch.randn((1, P, W0), generator=g, device=dev).half()
+        keys = torch.empty(kv, device=dev)
+        values = torch.empty(kv, device=dev, dtype=torch.float16)
+
+        def once():
+            rt.prefill(prefix, pm, keys=keys, values=values)
+    else:
+        keys = torch.randn(kv, generator=g, device=dev) * 0.5
+        values = (torch.randn(kv, generator=g, device=dev) * 0.5).half()
+        c, s_ = make_rope_np(S, vlm.head_dim, cfg.rope_theta, offset=P)
+        sc, ss = torch.from_numpy(c).to(dev), torch.from_numpy(s_).to(dev)
+        te = torch.from_numpy(make_time_embs(1, cfg.action_expert.width)[0]).to(dev, torch.float16)
+        x = torch.randn((1, S, D), generator=g, device=dev)
+        v = torch.empty_like(x)
+
+        def once():
+            rt.denoise_step_kv(keys, values, x, te, sc, ss, pm, out=v)
+    for _ in range(args.warmup):
+        once()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        once()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / max(1, args.steps)
+    print(json.dumps({"part": args.part, "ms": ms, "steps": args.steps, "warmup": args.warmup,
+                      "config": "pi0.5 fp16 batch 1 (full size)"}), flush=True)
+    rt.close()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--part", default="chunk", choices=["chunk", "prefill", "step"],
+                    help="profiling aid: time only the prefill or one denoise step")
     args = ap.parse_args()
+    if args.part != "chunk":
+        return run_part(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_b200(args)
