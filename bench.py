@@ -267,6 +267,7 @@ def run_b200(args):
     import torch.distributed as dist
 
     from mlc_vla import _lib
+    from mlc_vla.replicas import whole_job_throughput
     from mlc_vla.sample import PiZeroRunner, make_prefix_mask_np, make_rope_np, make_time_embs
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -351,12 +352,9 @@ def run_b200(args):
     n_launch = lib.pi0_launch_count(rt._ctx) - n0
     elapsed = e0.elapsed_time(e1)
     barrier()
-    t = torch.tensor([elapsed], device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    elapsed_max = float(t.item())
+    # whole-job chunks/s: every rank's chunks over the slowest rank's device time
+    value, elapsed_max = whole_job_throughput(elapsed, B * args.steps)
     ms_chunk = elapsed_max / args.steps
-    value = world * B * args.steps / (elapsed_max / 1e3)
 
     # end to end through the public API: pinned host prefix + noise up, actions down
     e2e = None
@@ -373,14 +371,11 @@ def run_b200(args):
             runner.sample_graph(params, host_prefix, noise=host_noise)
         f1.record(stream)
         torch.cuda.synchronize(dev)
-        te2e = torch.tensor([f0.elapsed_time(f1)], device=dev)
-        if world > 1:
-            dist.all_reduce(te2e, op=dist.ReduceOp.MAX)
+        e2e_value, e2e_ms = whole_job_throughput(f0.elapsed_time(f1), B * args.steps)
         h2d = (host_prefix.numel() * host_prefix.element_size() + host_noise.nbytes
                + B * P * 4 + 2 * B * S * (cfg.vlm.head_dim // 2) * 4
                + cfg.num_denoise_steps * cfg.action_expert.width * 2)
-        e2e = {"value": world * B * args.steps / (float(te2e.item()) / 1e3), "unit": "chunks/s",
-               "ms_per_step": float(te2e.item()) / args.steps,
+        e2e = {"value": e2e_value, "unit": "chunks/s", "ms_per_step": e2e_ms / args.steps,
                "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(B * S * D * 4)}
 
     # roofline of the dominant kernel family
