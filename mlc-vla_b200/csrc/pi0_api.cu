@@ -52,6 +52,7 @@ struct Entry {
   Role role;
   int expert;
   int layer;  // layer index, or modulation block for R_MOD_*
+  int in_dim = 0;  // quantised Linear entries: the unpadded input width K
 };
 
 struct LayerW {
@@ -110,6 +111,8 @@ struct pi0_ctx {
   bool attn_tc = false;
   void *q16p = nullptr, *q16s = nullptr, *kpre16 = nullptr, *ksuf16 = nullptr;
   bool pdl_barrier = false;  // the next launch waits for full completion of the previous one
+  void* qscratch = nullptr;  // quantised parameters: one dequantised Linear at a time
+  size_t qscratch_elems = 0;
   void *t1 = nullptr, *cond = nullptr, *mods = nullptr;
   float* splitk_ws = nullptr;
   size_t splitk_floats = 0;
@@ -256,8 +259,8 @@ void build_table(pi0_ctx* c) {
       c->table.push_back({name + ".weight", 2, {out, in}, dt, rw, e, l});
     } else {
       int64_t ng = (in + G - 1) / G;
-      c->table.push_back({name + ".q_weight", 2, {out, ng * (G / epw)}, PI0_U32, rw, e, l});
-      c->table.push_back({name + ".q_scale", 2, {out, ng}, dt, rw, e, l});
+      c->table.push_back({name + ".q_weight", 2, {out, ng * (G / epw)}, PI0_U32, rw, e, l, in});
+      c->table.push_back({name + ".q_scale", 2, {out, ng}, dt, rw, e, l, in});
     }
     if (bias) c->table.push_back({name + ".bias", 1, {out, 0}, dt, rb, e, l});
   };
@@ -1086,11 +1089,34 @@ int alloc_all(pi0_ctx* ctx) {
   TRY(dev_alloc(ctx, (void**)&ctx->tickets, (1 << 16) * 4));
   CK(cudaMemset(ctx->tickets, 0, (1 << 16) * 4));
   TRY(dev_alloc(ctx, (void**)&ctx->dev_err, 16));
+  if (g.quant != PI0_QUANT_NONE) {
+    // the widest Linear: gate_up of either expert, the modulations, or the projections
+    size_t mx = std::max(2 * F0 * W0, 2 * F1 * W1);
+    mx = std::max(mx, std::max((hq + 2 * hkv) * std::max(W0, W1), 3 * W1 * W1));
+    mx = std::max(mx, std::max(W0 * F0, W1 * F1));
+    ctx->qscratch_elems = mx;
+    TRY(dev_alloc(ctx, &ctx->qscratch, mx * e));
+  }
   ctx->ssq_parts = ssq_slots(ctx->cfg);
   if (ctx->ssq_parts > sk::SSQ_MAX_PARTS)
     return fail(ctx, PI0_ERR_UNSUPPORTED, "action-expert width too large for the row-sum partials");
   TRY(dev_alloc(ctx, (void**)&ctx->ssq, MS * ctx->ssq_parts * 4));
   CK(cudaMemset(ctx->dev_err, 0, 16));
+  return 0;
+}
+
+template <typename T>
+int dequant_into(pi0_ctx* ctx, int quant, const uint32_t* qw, const T* scale, int64_t n_out,
+                 int64_t k, T* out, cudaStream_t st) {
+  if (!qw) return fail(ctx, PI0_ERR_INVALID, "q_scale without its q_weight");
+  if ((size_t)(n_out * k) > ctx->qscratch_elems)
+    return fail(ctx, PI0_ERR_INVALID, "dequantisation scratch too small");
+  const int G = quant == PI0_QUANT_Q3 ? 40 : 32, bits = quant == PI0_QUANT_Q3 ? 3 : 4;
+  const int epw = quant == PI0_QUANT_Q3 ? 10 : 8, maxint = quant == PI0_QUANT_Q3 ? 3 : 7;
+  const int64_t n = n_out * k;
+  dequantize_kernel<T><<<(unsigned)((n + 255) / 256), 256, 0, st>>>(qw, scale, n_out, k, G, bits, epw,
+                                                                    maxint, out);
+  CKL();
   return 0;
 }
 
@@ -1103,10 +1129,24 @@ int set_params_impl(pi0_ctx* ctx, const void* const* params, cudaStream_t st) {
   const size_t F[2] = {(size_t)g.vlm_mlp_dim, (size_t)g.ae_mlp_dim};
   const size_t e = sizeof(T);
   const size_t W1 = g.ae_width;
+  const uint32_t* qw = nullptr;  // q_weight of the quantised Linear whose q_scale comes next
   for (size_t i = 0; i < ctx->table.size(); ++i) {
     const Entry& en = ctx->table[i];
     const void* src = params[i];
     if (!src) return fail(ctx, PI0_ERR_INVALID, "null pointer for parameter " + en.name);
+    if (en.dtype == PI0_U32) {
+      qw = static_cast<const uint32_t*>(src);
+      continue;
+    }
+    if (en.in_dim > 0) {
+      // quantised Linear: w = (code − max_int)·scale in the model dtype, then the same re-layout
+      // as an unquantised weight
+      const int quant = g.quant;
+      TRY(dequant_into<T>(ctx, quant, qw, static_cast<const T*>(src), en.shape[0], en.in_dim,
+                          (T*)ctx->qscratch, st));
+      src = ctx->qscratch;
+      qw = nullptr;
+    }
     const int l = en.layer, ex = en.expert;
     LayerW* lw = nullptr;
     if (en.role <= R_D) lw = ex == 0 ? &ctx->pre[l] : &ctx->suf[l];
@@ -1226,8 +1266,6 @@ int pi0_create(const pi0_config* cfg, int device, pi0_ctx** out) {
   ctx->esz = 2;
   build_table(ctx);
   *out = ctx;
-  if (cfg->quant != PI0_QUANT_NONE)
-    return fail(ctx, PI0_ERR_UNSUPPORTED, "quantised weights are not implemented in this build yet");
   CK(cudaSetDevice(device));
   int sms = 0;
   CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));

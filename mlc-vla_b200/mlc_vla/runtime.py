@@ -78,6 +78,8 @@ def to_device(x, dtype: str, device) -> torch.Tensor:
         a = np.asarray(x)
         if a.dtype == np.float16 and dtype != "float16":
             a = a.astype(np.float32)
+        if a.dtype == np.uint32:  # packed quantisation codes: keep the bits (int32 storage)
+            a = a.view(np.int32)
         t = torch.from_numpy(np.ascontiguousarray(a))
     return t.to(device=device, dtype=TORCH_DTYPE[dtype]).contiguous()
 
