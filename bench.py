@@ -300,10 +300,18 @@ def run_b200(args):
     P, S, D, W0 = cfg.prefix_len, cfg.suffix_len, cfg.action_dim, cfg.vlm.width
     prefix = torch.randn((B, P, W0), generator=gen, device=dev).to(torch.float16)
     noise = torch.randn((B, S, D), generator=gen, device=dev)
-    pm = torch.from_numpy(np.concatenate([make_prefix_mask_np(P)] * B, 0)).to(dev)
-    c, s = make_rope_np(S, cfg.vlm.head_dim, cfg.rope_theta, offset=P)
-    sc = torch.from_numpy(np.concatenate([c] * B, 0)).to(dev)
-    ss = torch.from_numpy(np.concatenate([s] * B, 0)).to(dev)
+    # --pad: per-request valid prefix length ~ U[700, 968] (seeded per rank), padded to 968 with
+    # the mask, suffix RoPE offset = valid length (the throughput sweep's inputs)
+    if args.pad:
+        nvs = np.random.default_rng(2000 + rank).integers(700, P + 1, size=B)
+    else:
+        nvs = np.full(B, P)
+    pads = np.stack([(np.arange(P) < nv).astype(np.float32) for nv in nvs])
+    pm = torch.from_numpy(np.concatenate(
+        [make_prefix_mask_np(P, pad_mask=pads[i]) for i in range(B)], 0)).to(dev)
+    ropes = [make_rope_np(S, cfg.vlm.head_dim, cfg.rope_theta, offset=int(nv)) for nv in nvs]
+    sc = torch.from_numpy(np.concatenate([r[0] for r in ropes], 0)).to(dev)
+    ss = torch.from_numpy(np.concatenate([r[1] for r in ropes], 0)).to(dev)
     te = torch.from_numpy(np.concatenate(make_time_embs(cfg.num_denoise_steps, cfg.action_expert.width), 0)).to(dev, torch.float16)
     vlm = cfg.vlm
     kv_shape = (vlm.depth, B, vlm.num_kv_heads, P, vlm.head_dim)
@@ -362,13 +370,13 @@ def run_b200(args):
         host_prefix = prefix.cpu().pin_memory()
         host_noise = noise.cpu().numpy()
         for _ in range(max(1, args.warmup)):
-            runner.sample_graph(params, host_prefix, noise=host_noise)
+            runner.sample_graph(params, host_prefix, noise=host_noise, prefix_pad=pads if args.pad else None)
         torch.cuda.synchronize(dev)
         barrier()
         f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         f0.record(stream)
         for _ in range(args.steps):
-            runner.sample_graph(params, host_prefix, noise=host_noise)
+            runner.sample_graph(params, host_prefix, noise=host_noise, prefix_pad=pads if args.pad else None)
         f1.record(stream)
         torch.cuda.synchronize(dev)
         e2e_value, e2e_ms = whole_job_throughput(f0.elapsed_time(f1), B * args.steps)
@@ -421,7 +429,9 @@ def run_b200(args):
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
             "data": "synthetic (random N(0,0.02) weights, N(0,1) prefix_embs and noise, seeded)",
             "config": {"workload": "pi0.5 fp16, per GPU batch %d: prefill(968) + denoise_loop_kv "
-                                   "(10 Euler steps, one CUDA graph); horizon 50, action_dim 32" % B,
+                                   "(10 Euler steps, one CUDA graph); horizon 50, action_dim 32%s"
+                                   % (B, "; valid prefix lengths U[700,968], padded with the mask"
+                                      if args.pad else ""),
                        "model": "pi0.5 (gemma_2b prefix expert + gemma_300m action expert)",
                        "global_batch": world * B, "seq_len": P, "parallelism": f"dp{world} (replicas)",
                        "l2": "inputs larger than L2 (4.8 GB of weights streamed per chunk)"},
@@ -495,6 +505,8 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--pad", action="store_true",
+                    help="per-request valid prefix lengths U[700,968] padded to 968 (throughput sweep)")
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")

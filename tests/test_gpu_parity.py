@@ -215,3 +215,28 @@ def test_gpu_quantiser_bit_exact(preset):
     assert np.array_equal(qs.float().cpu().numpy(), os_)
     dq = q.dequantize(qw, qs, 1000)
     assert np.array_equal(dq.float().cpu().numpy(), Q.dequantize(oq, os_, preset, 1000))
+
+
+def test_batch_beyond_weight_streaming_rows():
+    """20 padded requests in one call: 20·S = 160 activation rows in the denoise step, more than
+    the weight-streaming GEMM takes (128), so the tile GEMM with a separate norm runs instead.
+    Every request (own prefix, pad mask and suffix RoPE offset) is checked against the oracle."""
+    cfg = config(recipes.MINI)
+    b = 20
+    m = Model(cfg, max_batch=b)
+    inp = m.inputs(seed=5, batch=b)
+    rng = np.random.default_rng(9)
+    nvs = [int(v) for v in rng.integers(cfg.prefix_len // 2, cfg.prefix_len + 1, size=b)]
+    pm = np.concatenate([O.prefix_mask(cfg.prefix_len, nv) for nv in nvs], 0)
+    rope = [O.suffix_rope(cfg, nv) for nv in nvs]
+    sc = np.concatenate([r[0] for r in rope], 0)
+    ss = np.concatenate([r[1] for r in rope], 0)
+    te = O.time_embs(cfg.num_denoise_steps, cfg.action_expert.width)
+    k, v = m.rt.prefill(inp["prefix"], pm)
+    xb = _np(m.rt.denoise_loop_kv(k, v, inp["noise"], te, sc, ss, pm))
+    assert m.rt.device_error() == 0
+    for i in (0, 7, 19):
+        ko, vo = m.oracle_kv(inp["prefix"][i:i + 1], pm[i:i + 1])
+        xo = O.denoise_loop_kv(m.p, cfg, ko, vo, inp["noise"][i:i + 1], te, sc[i:i + 1],
+                               ss[i:i + 1], pm[i:i + 1])
+        _check(xb[i:i + 1], xo, what=f"batch-20 request {i} (valid {nvs[i]})")
