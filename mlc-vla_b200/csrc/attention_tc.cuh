@@ -397,15 +397,11 @@ __global__ void __launch_bounds__(NT, 1)
     // one (row, 4 dims) item per thread and pass; the nsplit partials of an item are loaded
     // together (static indices, predicated), then summed in rank order
     const int items = (rend - rbeg) * (HD / 4);
-#pragma unroll 1
-    for (int it = tid; it < items; it += NT) {
+    // two items per pass, the 2·nsplit loads of both issued together: each pass costs one
+    // round trip over the cluster
+    auto finish = [&](int it, const float4 (&v)[16]) {
       const int rr = it / (HD / 4), d = (it % (HD / 4)) * 4;
-      const int row = rbeg + rr, j = row0 + row;
-      const uint32_t off = oaddr + (row * S::OLD + d) * 4;
-      float4 v[16];
-#pragma unroll
-      for (int c = 0; c < 16; ++c)
-        if (c < nsplit) v[c] = ld_cluster4(map_rank(off, c));
+      const int j = row0 + rbeg + rr;
       float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
       for (int c = 0; c < 16; ++c)
@@ -422,6 +418,22 @@ __global__ void __launch_bounds__(NT, 1)
         *reinterpret_cast<uint2*>(out) =
             make_uint2(Tr<__half>::pack(acc.x * inv, acc.y * inv), Tr<__half>::pack(acc.z * inv, acc.w * inv));
       }
+    };
+    auto load = [&](int it, float4 (&v)[16]) {
+      const int rr = it / (HD / 4), d = (it % (HD / 4)) * 4;
+      const uint32_t off = oaddr + ((rbeg + rr) * S::OLD + d) * 4;
+#pragma unroll
+      for (int c = 0; c < 16; ++c)
+        if (c < nsplit) v[c] = ld_cluster4(map_rank(off, c));
+    };
+#pragma unroll 1
+    for (int it = tid; it < items; it += 2 * NT) {
+      float4 v0[16], v1[16];
+      const bool two = it + NT < items;
+      load(it, v0);
+      if (two) load(it + NT, v1);
+      finish(it, v0);
+      if (two) finish(it + NT, v1);
     }
     cluster_sync();  // peers may still read this CTA's partial
   }
