@@ -20,7 +20,8 @@ def rt():
 @pytest.mark.parametrize("m,n,k", [(128, 256, 64), (968, 2560, 2048), (200, 160, 320),
                                    (50, 1024, 4096), (777, 390, 96), (1000, 32768, 128),
                                    (50, 2560, 1024), (50, 8192, 1024), (50, 1024, 2048),
-                                   (100, 160, 200), (8, 384, 128), (1, 3072, 1024)])
+                                   (100, 160, 200), (8, 384, 128), (1, 3072, 1024),
+                                   (968, 2048, 16384), (300, 1000, 4160)])
 def test_linear_matches_torch_fp32(rt, engine, m, n, k):
     if engine == 2 and k % 32:
         pytest.skip("warp-level engine needs K % 32 == 0")
