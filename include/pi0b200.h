@@ -148,6 +148,13 @@ int pi0_linear_noalloc(int dtype, const void* x, int M, int K, const void* w, in
  * bounded wait inside a kernel gave up. */
 int pi0_device_error(pi0_ctx* ctx);
 
+/* Bounded-wait check (no counterpart in the reference): one device thread waits on a barrier
+ * phase with the bounded wait all kernels here use. The phase completes only when `arrive` is
+ * nonzero; otherwise the wait gives up after about one second, stores 3 (timeout) into the
+ * device int *err if it is still 0, and the kernel returns, leaving the context usable. Lets
+ * tests exercise the failure path without faulting or hanging a GPU. Context-free. */
+int pi0_wait_check(int* err, int arrive, pi0_stream_t stream);
+
 /* out[i] = a[i] / b[i] (fp32, n elements, device pointers) computed by the reciprocal-and-
  * correction sequence the norm-fused projections use for x / sqrt(mean(x²) + eps); exposed so
  * tests can compare it with IEEE division bit for bit. Context-free. */

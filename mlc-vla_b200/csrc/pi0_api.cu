@@ -1497,6 +1497,25 @@ int pi0_linear(pi0_ctx* ctx, const void* x, int M, int K, const void* w, int N, 
                  stream, F_PRE_QKV, engine);
 }
 
+// One thread waits, through the same bounded mbarrier wait every kernel here uses, on a phase
+// that completes only if `arrive` is nonzero: with no arrival the wait gives up after about a
+// second and records ERR_TIMEOUT_EPI in *err, and the kernel returns normally.
+__global__ void wait_check_kernel(int* err, int arrive) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    tc::mbar_init(&bar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    if (arrive) tc::mbar_arrive(&bar);
+    tc::mbar_wait(&bar, 0, err, tc::ERR_TIMEOUT_EPI, false);
+  }
+}
+
+int pi0_wait_check(int* err, int arrive, pi0_stream_t stream) {
+  if (!err) return PI0_ERR_INVALID;
+  wait_check_kernel<<<1, 32, 0, stream>>>(err, arrive);
+  return cudaGetLastError() == cudaSuccess ? 0 : PI0_ERR_CUDA;
+}
+
 int pi0_div_check(const float* a, const float* b, float* out, int64_t n, pi0_stream_t stream) {
   if (!a || !b || !out || n < 0) return PI0_ERR_INVALID;
   if (n == 0) return 0;
