@@ -262,6 +262,45 @@ def make_weights(named_params, device, seed=0):
     return out
 
 
+def family_times(rt, fn):
+    """{kernel family: (launches, device ms)} of one call of `fn`, replayed from a captured graph
+    in which every launch is bracketed by event-record nodes (the profiled pass)."""
+    import ctypes
+
+    import torch
+
+    from mlc_vla import _lib
+
+    lib = _lib.load()
+    lib.pi0_profile_enable(rt._ctx, 1)
+    fn()
+    torch.cuda.synchronize()
+    nf = lib.pi0_profile_families()
+    launches = (ctypes.c_int64 * nf)()
+    total = (ctypes.c_double * nf)()
+    _lib.check(lib.pi0_profile_read(rt._ctx, nf, launches, total), rt._ctx)
+    lib.pi0_profile_enable(rt._ctx, 0)
+    return {lib.pi0_profile_family_name(i).decode(): (int(launches[i]), float(total[i]))
+            for i in range(nf) if launches[i]}
+
+
+def make_quant_weights(cfg, preset, device, seed=0):
+    """The quantised parameter table of `preset` (q_weight, q_scale and bias per Linear): the
+    make_weights draws, each Linear weight group-quantised on the GPU."""
+    from mlc_vla.model.pi0.pi0_model import backbone_named_params
+    from mlc_vla.runtime import quantize_weight
+
+    fp = dict(zip([n for n, _ in backbone_named_params(cfg)],
+                  make_weights(backbone_named_params(cfg), device, seed)))
+    out = []
+    for name, _ in backbone_named_params(cfg, quant=preset):
+        if name.endswith(".q_weight"):
+            out += quantize_weight(fp[name[: -len(".q_weight")] + ".weight"], preset)
+        elif not name.endswith(".q_scale"):
+            out.append(fp[name])
+    return out
+
+
 def run_b200(args):
     import torch
     import torch.distributed as dist
@@ -328,20 +367,7 @@ def run_b200(args):
         chunk()
     torch.cuda.synchronize(dev)
 
-    # per-kernel-family device times (profiled pass: the chunk replayed from a captured graph in
-    # which every launch is bracketed by event-record nodes)
-    lib.pi0_profile_enable(rt._ctx, 1)
-    chunk()
-    torch.cuda.synchronize(dev)
-    nf = lib.pi0_profile_families()
-    import ctypes
-
-    launches = (ctypes.c_int64 * nf)()
-    total = (ctypes.c_double * nf)()
-    _lib.check(lib.pi0_profile_read(rt._ctx, nf, launches, total), rt._ctx)
-    lib.pi0_profile_enable(rt._ctx, 0)
-    fam = {lib.pi0_profile_family_name(i).decode(): (int(launches[i]), float(total[i]))
-           for i in range(nf) if launches[i]}
+    fam = family_times(rt, chunk)
     for _ in range(2):
         chunk()  # re-warm the graph path
     torch.cuda.synchronize(dev)
@@ -458,8 +484,15 @@ def run_part(args):
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     cfg = full_config()
-    rt = Pi0Runtime(cfg, device=0)
-    rt.bind(make_weights(rt.named_params, dev, seed=0))
+    if args.quant != "none":
+        from mlc_vla.quant import PRESETS
+
+        q = PRESETS[args.quant]
+        rt = Pi0Runtime(cfg, device=0, quant=q)
+        rt.bind(rt.to_params(make_quant_weights(cfg, q, dev, seed=0)))
+    else:
+        rt = Pi0Runtime(cfg, device=0)
+        rt.bind(make_weights(rt.named_params, dev, seed=0))
     P, S, D, W0 = cfg.prefix_len, cfg.suffix_len, cfg.action_dim, cfg.vlm.width
     g = torch.Generator(device=dev).manual_seed(1)
     pm = torch.from_numpy(make_prefix_mask_np(P)).to(dev)
@@ -486,6 +519,10 @@ def run_part(args):
     for _ in range(args.warmup):
         once()
     torch.cuda.synchronize(dev)
+    fam = family_times(rt, once)
+    for _ in range(2):
+        once()
+    torch.cuda.synchronize(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(args.steps):
@@ -494,7 +531,10 @@ def run_part(args):
     torch.cuda.synchronize(dev)
     ms = e0.elapsed_time(e1) / max(1, args.steps)
     print(json.dumps({"part": args.part, "ms": ms, "steps": args.steps, "warmup": args.warmup,
-                      "config": "pi0.5 fp16 batch 1 (full size)"}), flush=True)
+                      "config": f"pi0.5 fp16 batch 1 (full size), weights {args.quant}",
+                      "families_ms": {k: round(v[1], 4) for k, v in sorted(
+                          fam.items(), key=lambda kv: -kv[1][1])}}),
+          flush=True)
     rt.close()
     return 0
 
@@ -512,6 +552,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--part", default="chunk", choices=["chunk", "prefill", "step"],
                     help="profiling aid: time only the prefill or one denoise step")
+    ap.add_argument("--quant", default="none", choices=["none", "q4f16_1", "q3f16_1"],
+                    help="with --part: group-quantised weights (fused dequant in the denoise GEMMs)")
     args = ap.parse_args()
     if args.part != "chunk":
         return run_part(args)

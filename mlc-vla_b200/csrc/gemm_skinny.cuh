@@ -124,6 +124,154 @@ __global__ void pack_sw128_kernel(uint16_t* __restrict__ dst, const uint16_t* __
   *reinterpret_cast<uint4*>(dst + ((t * nkb + kb) * BM + r) * BK + cs * 8) = v;
 }
 
+// Group-quantised weight blocks, in the same (tile, k-block) order as the 16-bit packed blocks,
+// qw_block(QB) bytes per 128×64 block. Chunk c of a row = columns 8c..8c+7 of the block; pair h
+// of a chunk = columns 8c+2h, 8c+2h+1. The codes are re-ordered at bind time so that one shift
+// and one mask put a pair's two codes at bits 0 and 16 of a register:
+//   q4 (q4f16_1 / q4bf16_1: G = 32, w = (code − 7)·s): [128 rows × 8 words], word c of a row
+//      holds chunk c with the code of column 2h at bits 4h and of column 2h+1 at bits 16 + 4h;
+//      then [128 rows × 2 scales] (columns 0-31, 32-63). 4608 bytes.
+//   q3 (q3f16_1: G = 40, w = (code − 3)·s): low two bits of every code in [128 rows × 4 words]
+//      (chunk c, pair h at bits 8·(c&1) + 2h and +16 of word c>>1), the third bit in
+//      [128 rows × 2 words] (pair p = 4c + h at bit p&15 and +16 of word p>>4), then
+//      [128 rows × 4 scales]: the three groups a 64-wide block can touch (groups start at
+//      multiples of 40, always on a chunk boundary) and a zero pad. 4096 bytes.
+// The kernel loads a block into the tail of the stage's weight slot and dequantises it in place
+// into the 16 KB swizzled image the MMA reads.
+__host__ __device__ constexpr int qw_block(int qb) { return qb == 4 ? BM * 36 : BM * 32; }
+__host__ __device__ constexpr int qw_off(int qb) { return W_BLOCK - qw_block(qb); }
+
+// Packs rows [row0, row0 + n) of a fused matrix from one quantised Linear (reference layout:
+// q_weight [.., ceil(K/G)·G/epw] uint32 with code k at word k/epw, bits bits·(k%epw); q_scale
+// [.., ceil(K/G)] 16-bit): destination row row0 + r takes source row idx ? idx[r] : r.
+// K % 64 == 0. One thread per (row, k-block), scalar loads (the caller's buffers need only their
+// natural alignment); rows past the matrix stay as the caller zeroed them.
+template <int QB>
+__global__ void pack_q_kernel(uint8_t* __restrict__ dst, const uint32_t* __restrict__ qw,
+                              const uint16_t* __restrict__ qs, const int* __restrict__ idx, int n,
+                              int K, int row0, int nkb) {
+  const int id = blockIdx.x * blockDim.x + threadIdx.x;
+  const int rl = id / nkb, kb = id - rl * nkb;
+  if (rl >= n) return;
+  const int src = idx ? idx[rl] : rl;
+  const int r = row0 + rl, rr = r % BM;
+  uint8_t* blk = dst + ((size_t)(r / BM) * nkb + kb) * qw_block(QB);
+  if constexpr (QB == 4) {
+    const uint32_t* w = qw + (size_t)src * (K / 8) + kb * 8;
+    uint32_t* oc = reinterpret_cast<uint32_t*>(blk + rr * 32);
+    for (int c = 0; c < 8; ++c) {
+      const uint32_t v = w[c];  // column 8c + j at bits 4j
+      uint32_t o = 0;
+      for (int h = 0; h < 4; ++h)
+        o |= ((v >> (8 * h)) & 15u) << (4 * h) | ((v >> (8 * h + 4)) & 15u) << (16 + 4 * h);
+      oc[c] = o;
+    }
+    const uint16_t* sc = qs + (size_t)src * (K / 32) + kb * 2;
+    uint16_t* os = reinterpret_cast<uint16_t*>(blk + BM * 32 + rr * 4);
+    os[0] = sc[0];
+    os[1] = sc[1];
+  } else {
+    const int ng = (K + 39) / 40;
+    const uint32_t* w = qw + (size_t)src * ng * 4;
+    uint32_t lo[4] = {0, 0, 0, 0}, hi[2] = {0, 0};
+    for (int c = 0; c < 8; ++c)
+      for (int h = 0; h < 4; ++h)
+        for (int e = 0; e < 2; ++e) {
+          const int k = kb * 64 + 8 * c + 2 * h + e;
+          const uint32_t code = (w[k / 10] >> (3 * (k % 10))) & 7u;
+          lo[c >> 1] |= (code & 3u) << (8 * (c & 1) + 2 * h + 16 * e);
+          const int p = 4 * c + h;
+          hi[p >> 4] |= (code >> 2) << ((p & 15) + 16 * e);
+        }
+    uint32_t* ol = reinterpret_cast<uint32_t*>(blk + rr * 16);
+    uint32_t* oh = reinterpret_cast<uint32_t*>(blk + BM * 16 + rr * 8);
+    for (int j = 0; j < 4; ++j) ol[j] = lo[j];
+    oh[0] = hi[0];
+    oh[1] = hi[1];
+    uint16_t* os = reinterpret_cast<uint16_t*>(blk + BM * 24 + rr * 8);
+    const int g0 = kb * 64 / 40;
+    for (int t = 0; t < 3; ++t) os[t] = g0 + t < ng ? qs[(size_t)src * ng + g0 + t] : (uint16_t)0;
+    os[3] = 0;
+  }
+}
+
+// Two codes (bits 0-3 and 16-19 of x, higher bits clear) -> the model-dtype pair
+// RN((code − off)·g) = dequantize_kernel's arithmetic. fp16: x | 0x6400 is the half 1024 + code,
+// so the subtraction is exact and the one rounding is the half multiply's (the exact product
+// rounded to nearest, as the fp32 product rounded to half is). bf16: the same in fp32 through
+// 2^23 + code, then one rounding to bf16.
+template <typename T, int OFF>
+__device__ __forceinline__ uint32_t dequant_pair(uint32_t x, uint32_t g2, float g) {
+  if constexpr (Tr<T>::kBf16) {
+    const float a = __uint_as_float(0x4B000000u | (x & 0xFFFFu)) - (8388608.f + OFF);
+    const float b = __uint_as_float(0x4B000000u | (x >> 16)) - (8388608.f + OFF);
+    return Tr<T>::pack(a * g, b * g);
+  } else {
+    const uint32_t v = x | 0x64006400u;
+    const __half2 c = __hsub2(*reinterpret_cast<const __half2*>(&v),
+                              __halves2half2(__ushort_as_half((unsigned short)(0x6400 + OFF)),
+                                             __ushort_as_half((unsigned short)(0x6400 + OFF))));
+    const __half2 r = __hmul2(c, *reinterpret_cast<const __half2*>(&g2));
+    return *reinterpret_cast<const uint32_t*>(&r);
+  }
+}
+
+// Dequantises the block at `slot + qw_off(QB)` (k-block kb of the matrix) into the swizzled
+// K-major image at `slot` (row r, 16-byte chunk c at r·128 + ((c ^ (r & 7))·16)). Worker thread
+// wt owns row wt; every thread reads its inputs before any writes (the output overlaps the
+// input), hence the barrier in the middle.
+template <typename T, int QB>
+__device__ __forceinline__ void dequant_inplace(uint8_t* slot, int wt, int kb) {
+  const uint8_t* blk = slot + qw_off(QB);
+  uint32_t cw[8];        // q4: one word per chunk; q3: low planes 0-3, high planes 4-5
+  uint16_t sraw[3];      // the block's scales, raw
+  if constexpr (QB == 4) {
+    const uint4 c0 = reinterpret_cast<const uint4*>(blk + wt * 32)[0];
+    const uint4 c1 = reinterpret_cast<const uint4*>(blk + wt * 32)[1];
+    cw[0] = c0.x; cw[1] = c0.y; cw[2] = c0.z; cw[3] = c0.w;
+    cw[4] = c1.x; cw[5] = c1.y; cw[6] = c1.z; cw[7] = c1.w;
+    const uint32_t sc = *reinterpret_cast<const uint32_t*>(blk + BM * 32 + wt * 4);
+    sraw[0] = (uint16_t)sc;
+    sraw[1] = (uint16_t)(sc >> 16);
+    sraw[2] = 0;
+  } else {
+    const uint4 l = *reinterpret_cast<const uint4*>(blk + wt * 16);
+    const uint2 h = *reinterpret_cast<const uint2*>(blk + BM * 16 + wt * 8);
+    const uint2 sc = *reinterpret_cast<const uint2*>(blk + BM * 24 + wt * 8);
+    cw[0] = l.x; cw[1] = l.y; cw[2] = l.z; cw[3] = l.w;
+    cw[4] = h.x; cw[5] = h.y; cw[6] = 0u; cw[7] = 0u;
+    sraw[0] = (uint16_t)sc.x;
+    sraw[1] = (uint16_t)(sc.x >> 16);
+    sraw[2] = (uint16_t)sc.y;
+  }
+  workers_sync();
+  const int r0 = (kb * 64) % 40;  // q3: column of the block's first element inside its group
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    int gi;
+    if constexpr (QB == 4) gi = c >> 2;
+    else gi = (r0 + 8 * c) / 40;
+    const uint16_t sb = gi == 0 ? sraw[0] : (gi == 1 ? sraw[1] : sraw[2]);
+    const uint32_t g2 = (uint32_t)sb * 0x10001u;  // the scale in both halves
+    const float g = Tr<T>::f(*reinterpret_cast<const T*>(&sb));
+    uint32_t o[4];
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      if constexpr (QB == 4) {
+        o[h] = dequant_pair<T, 7>((cw[c] >> (4 * h)) & 0x000F000Fu, g2, g);
+      } else {
+        const uint32_t lo2 = (cw[c >> 1] >> (8 * (c & 1) + 2 * h)) & 0x00030003u;
+        const int p = 4 * c + h;
+        const uint32_t hi1 = ((cw[4 + (p >> 4)] >> (p & 15)) & 0x00010001u) << 2;
+        o[h] = dequant_pair<T, 3>(lo2 | hi1, g2, g);
+      }
+    }
+    *reinterpret_cast<uint4*>(slot + wt * 128 + ((c ^ (wt & 7)) << 4)) =
+        make_uint4(o[0], o[1], o[2], o[3]);
+  }
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 // NORM: normalises one raw x block in place. The block holds x[0:NA, 64 columns] as written by
 // TMA in the 128-byte swizzle layout (element (r, k) at r·128 + ((k/8) ^ (r & 7))·16 + (k%8)·2,
 // rows ≥ M and columns ≥ K zero-filled). Worker thread wt (0..127) owns 16-byte column chunk
@@ -164,7 +312,9 @@ __device__ __forceinline__ void norm_inplace(const SkArgs& a, uint8_t* xb, uint4
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-template <typename T, int NA, bool NORM, bool SSQ, class Epi>
+// QB: 0 = 16-bit weights (packed blocks or a tensor map), 4 / 3 = group-quantised blocks
+// (pack_q_kernel) dequantised in shared memory by the worker warps.
+template <typename T, int NA, bool NORM, bool SSQ, class Epi, int QB = 0>
 __global__ void __launch_bounds__(NT, 2) skinny_kernel(const __grid_constant__ CUtensorMap tmW,
                                                        const __grid_constant__ CUtensorMap tmX,
                                                        SkArgs a, Epi epi) {
@@ -172,7 +322,8 @@ __global__ void __launch_bounds__(NT, 2) skinny_kernel(const __grid_constant__ C
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
-  // full_w / full_x: TMA landed; ready_x (NORM): block normalised; empty: MMAs done with a stage
+  // full_w / full_x: copy landed; ready_x (NORM or QB): the stage's blocks are normalised /
+  // dequantised; empty: MMAs done with a stage
   __shared__ __align__(8) uint64_t full_w[RING], full_x[RING], ready_x[RING], empty[RING], bar_mma;
   __shared__ uint32_t s_tmem;
   __shared__ int s_ok, s_stop;
@@ -213,13 +364,15 @@ __global__ void __launch_bounds__(NT, 2) skinny_kernel(const __grid_constant__ C
   tc_fence_after();
   const uint32_t tmem = s_tmem;
 
+  constexpr int WB = QB ? qw_block(QB) : W_BLOCK;  // bytes of one weight block in global memory
   const uint8_t* wsrc =
-      a.wpack ? reinterpret_cast<const uint8_t*>(a.wpack) + ((size_t)tile * nkb + kb0) * W_BLOCK
+      a.wpack ? reinterpret_cast<const uint8_t*>(a.wpack) + ((size_t)tile * nkb + kb0) * WB
               : nullptr;
   auto issue_w = [&](int i) {
     const int s = i % RING;
-    mbar_expect_tx(&full_w[s], W_BLOCK);
-    if (wsrc) bulk_load(stage_w(s), wsrc + (size_t)i * W_BLOCK, W_BLOCK, &full_w[s]);
+    mbar_expect_tx(&full_w[s], WB);
+    if (QB) bulk_load(stage_w(s) + qw_off(QB), wsrc + (size_t)i * WB, WB, &full_w[s]);
+    else if (wsrc) bulk_load(stage_w(s), wsrc + (size_t)i * WB, WB, &full_w[s]);
     else tma_load_2d(stage_w(s), &tmW, &full_w[s], (kb0 + i) * BK, n0);
   };
 
@@ -228,6 +381,24 @@ __global__ void __launch_bounds__(NT, 2) skinny_kernel(const __grid_constant__ C
   if (tid == 0)
     for (; issued < min(nk, RING); ++issued) issue_w(issued);
   pdl_trigger();
+  // QB: the worker warps dequantise those first blocks while the previous kernel finishes (the
+  // weights do not depend on it); without NORM such a stage is then ready but for its x block
+  int pre = 0;
+  if constexpr (QB != 0) {
+    if (warp >= 2) {
+      const int wt = tid - 64;
+      for (; pre < min(nk, RING); ++pre) {
+        if (!mbar_wait(&full_w[pre], 0, a.err, ERR_TIMEOUT_EPI)) s_stop = 1;
+        workers_sync();
+        if (s_stop) break;
+        dequant_inplace<T, QB>(stage_w(pre), wt, kb0 + pre);
+        if constexpr (!NORM) {
+          workers_sync();
+          if (wt == 0) mbar_arrive(&ready_x[pre]);
+        }
+      }
+    }
+  }
   pdl_wait();
 
   // the epilogue's global operands (residual rows, gates, RoPE tables) do not depend on the
@@ -261,8 +432,9 @@ __global__ void __launch_bounds__(NT, 2) skinny_kernel(const __grid_constant__ C
       for (int i = 0; i < nk; ++i) {
         const int s = i % RING;
         const uint32_t ph = (i / RING) & 1;
-        if (!mbar_wait(&full_w[s], ph, a.err, ERR_TIMEOUT_MMA) ||
-            !mbar_wait(NORM ? &ready_x[s] : &full_x[s], ph, a.err, ERR_TIMEOUT_MMA))
+        if ((!QB && !mbar_wait(&full_w[s], ph, a.err, ERR_TIMEOUT_MMA)) ||
+            ((NORM || QB) && !mbar_wait(&ready_x[s], ph, a.err, ERR_TIMEOUT_MMA)) ||
+            (!NORM && !mbar_wait(&full_x[s], ph, a.err, ERR_TIMEOUT_MMA)))
           break;
         tc_fence_after();
         const uint64_t da = desc_sw128(smem_u32(stage_w(s)));
@@ -275,7 +447,8 @@ __global__ void __launch_bounds__(NT, 2) skinny_kernel(const __grid_constant__ C
       umma_commit(&bar_mma);  // arrives once every issued MMA is done (at once if none)
     }
   } else {
-    if (NORM) {  // warps 2-5: normalise each raw x block in place once its copy has landed
+    if (NORM || QB) {  // warps 2-5: per stage, dequantise the weight block (QB) and normalise
+                       // the raw x block (NORM) in place once their copies have landed
       const int wt = tid - 64;
       const T* mod = reinterpret_cast<const T*>(a.mod);
       const uint4 z = make_uint4(0, 0, 0, 0);
@@ -286,34 +459,50 @@ __global__ void __launch_bounds__(NT, 2) skinny_kernel(const __grid_constant__ C
         c2 = in ? *reinterpret_cast<const uint4*>(mod + a.K + col) : z;
       };
       uint4 sc = z, sh = z;
-      if (nk > 0) load_mod(0, sc, sh);
-      if (wt < a.M) {  // M ≤ NA ≤ 128: one row per thread; partials summed in slot order
-        const float4* p = reinterpret_cast<const float4*>(a.ssq_in + (size_t)wt * a.ssq_parts);
-        float ss = 0.f;
-        for (int i = 0; i < a.ssq_parts / 4; i += 4) {
-          float4 v[4];
+      if constexpr (NORM) {
+        if (nk > 0) load_mod(0, sc, sh);
+        if (wt < a.M) {  // M ≤ NA ≤ 128: one row per thread; partials summed in slot order
+          const float4* p = reinterpret_cast<const float4*>(a.ssq_in + (size_t)wt * a.ssq_parts);
+          float ss = 0.f;
+          for (int i = 0; i < a.ssq_parts / 4; i += 4) {
+            float4 v[4];
 #pragma unroll
-          for (int j = 0; j < 4; ++j) v[j] = p[i + j];
+            for (int j = 0; j < 4; ++j) v[j] = p[i + j];
 #pragma unroll
-          for (int j = 0; j < 4; ++j) ss = ((ss + v[j].x) + v[j].y + v[j].z) + v[j].w;
+            for (int j = 0; j < 4; ++j) ss = ((ss + v[j].x) + v[j].y + v[j].z) + v[j].w;
+          }
+          const float den = sqrtf(__fadd_rn(__fdiv_rn(ss, (float)a.K), a.eps));
+          s_den[wt] = den;
+          s_rcp[wt] = __frcp_rn(den);
         }
-        const float den = sqrtf(__fadd_rn(__fdiv_rn(ss, (float)a.K), a.eps));
-        s_den[wt] = den;
-        s_rcp[wt] = __frcp_rn(den);
+        workers_sync();
       }
-      workers_sync();
       for (int i = 0; i < nk; ++i) {
         const int s = i % RING;
-        uint4 nsc = z, nsh = z;
-        if (i + 1 < nk) load_mod(i + 1, nsc, nsh);
-        if (!mbar_wait(&full_x[s], (i / RING) & 1, a.err, ERR_TIMEOUT_EPI)) s_stop = 1;
-        workers_sync();
-        if (s_stop) break;
-        norm_inplace<T, NA>(a, stage_x(s), sc, sh, s_den, s_rcp, wt);
+        const uint32_t ph = (i / RING) & 1;
+        if (s_stop) break;  // a wait before the previous kernel's end gave up
+        if constexpr (QB != 0) {
+          if (i >= pre) {
+            if (!mbar_wait(&full_w[s], ph, a.err, ERR_TIMEOUT_EPI)) s_stop = 1;
+            workers_sync();
+            if (s_stop) break;
+            dequant_inplace<T, QB>(stage_w(s), wt, kb0 + i);
+          } else if (!NORM) {
+            continue;  // dequantised and marked ready before the wait
+          }
+        }
+        if constexpr (NORM) {
+          uint4 nsc = z, nsh = z;
+          if (i + 1 < nk) load_mod(i + 1, nsc, nsh);
+          if (!mbar_wait(&full_x[s], ph, a.err, ERR_TIMEOUT_EPI)) s_stop = 1;
+          workers_sync();
+          if (s_stop) break;
+          norm_inplace<T, NA>(a, stage_x(s), sc, sh, s_den, s_rcp, wt);
+          sc = nsc;
+          sh = nsh;
+        }
         workers_sync();
         if (wt == 0) mbar_arrive(&ready_x[s]);
-        sc = nsc;
-        sh = nsh;
       }
     }
   }

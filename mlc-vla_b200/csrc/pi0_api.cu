@@ -64,6 +64,9 @@ struct LayerW {
   void* ln_post;
   // action expert only: the same matrices packed for the weight-streaming GEMM
   void *qkv_p = nullptr, *o_p = nullptr, *gu_p = nullptr, *d_p = nullptr;
+  // quantised models: the same matrices as group-quantised blocks (pack_q_kernel layout), which
+  // the weight-streaming kernel dequantises in shared memory; null when not in use
+  void *qkv_q = nullptr, *o_q = nullptr, *gu_q = nullptr, *d_q = nullptr;
 };
 
 struct GraphKey {
@@ -93,6 +96,8 @@ struct pi0_ctx {
   void *ain_w = nullptr, *ain_b = nullptr, *aout_w = nullptr, *aout_b = nullptr;
   void *tin_w = nullptr, *tin_b = nullptr, *tout_w = nullptr, *tout_b = nullptr;
   void *mod_w_p = nullptr, *tin_p = nullptr, *tout_p = nullptr;  // packed copies
+  void *mod_w_q = nullptr, *tin_q = nullptr, *tout_q = nullptr;  // quantised blocks (qb != 0)
+  int qb = 0;  // 4 / 3: the weight-streaming GEMMs read q4 / q3 blocks; 0: 16-bit blocks
   float* ssq = nullptr;  // [max_batch·S][ssq_parts] row Σx² partials of the suffix stream
   int ssq_parts = 1;
   int* perm_q = nullptr;   // RoPE row permutation of a q block (H·hd rows)
@@ -409,7 +414,7 @@ struct SkOpt {
   const void* mod = nullptr;    // NORM: modulation row (scale | shift)
 };
 
-template <typename T, int NA, bool NORM, bool SSQ, class Epi>
+template <typename T, int NA, bool NORM, bool SSQ, int QB = 0, class Epi>
 int skinny_launch(pi0_ctx* ctx, const T* X, int ldx, const T* W, int ldw, int M, int N, int K,
                   const Epi& epi, cudaStream_t st, int fam, SkOpt o) {
   const int nkb = (K + 63) / 64, tiles = (N + 127) / 128;
@@ -426,21 +431,30 @@ int skinny_launch(pi0_ctx* ctx, const T* X, int ldx, const T* W, int ldw, int M,
   sk::SkArgs a{M, N, K, kbpc, C, ctx->dev_err, o.wpack, X, o.mod, ctx->cfg.rms_norm_eps,
                ctx->ssq, ctx->ssq, ctx->ssq_parts};
   Prof pr(ctx, fam, st);
-  return launch(ctx, sk::skinny_kernel<T, NA, NORM, SSQ, Epi>, dim3(tiles * C), dim3(sk::NT),
+  return launch(ctx, sk::skinny_kernel<T, NA, NORM, SSQ, Epi, QB>, dim3(tiles * C), dim3(sk::NT),
                 sk::SkSmem<NA>::BYTES, st, dim3(C, 1, 1), tw, tx, a, epi);
 }
 
-// Denoise-path projection: the weight-streaming kernel for M ≤ 128 (packed weights `Wp`),
-// the tensor-core tile kernel otherwise (row-major `W`). NORM: the input is adaRMSNorm(A; mod)
-// (fused for M ≤ 128, a separate norm kernel into `scratch` otherwise). SSQ: the epilogue also
-// emits the row Σx² partials of its output stream.
+// Denoise-path projection: the weight-streaming kernel for M ≤ 128 (group-quantised blocks `Wq`
+// when the context has them, else packed 16-bit weights `Wp`), the tensor-core tile kernel
+// otherwise (row-major `W`). NORM: the input is adaRMSNorm(A; mod) (fused for M ≤ 128, a
+// separate norm kernel into `scratch` otherwise). SSQ: the epilogue also emits the row Σx²
+// partials of its output stream.
 template <typename T, bool NORM, bool SSQ, class Epi>
-int gemm_w(pi0_ctx* ctx, const T* A, int lda, const T* W, const T* Wp, int M, int N, int K,
-           const Epi& epi, cudaStream_t st, int fam, const T* mod = nullptr,
+int gemm_w(pi0_ctx* ctx, const T* A, int lda, const T* W, const T* Wp, const void* Wq, int M,
+           int N, int K, const Epi& epi, cudaStream_t st, int fam, const T* mod = nullptr,
            T* scratch = nullptr) {
   SkOpt o;
   o.wpack = Wp;
   o.mod = mod;
+  if (M <= 128 && Wq && ctx->qb) {
+    o.wpack = Wq;
+    if (ctx->qb == 4)
+      return M <= 64 ? skinny_launch<T, 64, NORM, SSQ, 4>(ctx, A, lda, W, K, M, N, K, epi, st, fam, o)
+                     : skinny_launch<T, 128, NORM, SSQ, 4>(ctx, A, lda, W, K, M, N, K, epi, st, fam, o);
+    return M <= 64 ? skinny_launch<T, 64, NORM, SSQ, 3>(ctx, A, lda, W, K, M, N, K, epi, st, fam, o)
+                   : skinny_launch<T, 128, NORM, SSQ, 3>(ctx, A, lda, W, K, M, N, K, epi, st, fam, o);
+  }
   if (M <= 64) return skinny_launch<T, 64, NORM, SSQ>(ctx, A, lda, W, K, M, N, K, epi, st, fam, o);
   if (M <= 128) return skinny_launch<T, 128, NORM, SSQ>(ctx, A, lda, W, K, M, N, K, epi, st, fam, o);
   if (NORM) {
@@ -582,15 +596,15 @@ int time_and_mods(pi0_ctx* ctx, const T* te, int nsteps, cudaStream_t st) {
   for (int m0 = 0; m0 < nsteps; m0 += 64) {
     const int mm = std::min(64, nsteps - m0);
     TRY((gemm_w<T, false, false>(ctx, te + (size_t)m0 * W1, W1, (const T*)ctx->tin_w,
-                                 (const T*)ctx->tin_p, mm, W1, W1,
+                                 (const T*)ctx->tin_p, ctx->tin_q, mm, W1, W1,
                                  EpiStore<T>{t1 + (size_t)m0 * W1, W1, (const T*)ctx->tin_b, 1}, st,
                                  F_DEN_TIME_MODS)));
     TRY((gemm_w<T, false, false>(ctx, t1 + (size_t)m0 * W1, W1, (const T*)ctx->tout_w,
-                                 (const T*)ctx->tout_p, mm, W1, W1,
+                                 (const T*)ctx->tout_p, ctx->tout_q, mm, W1, W1,
                                  EpiStore<T>{cond + (size_t)m0 * W1, W1, (const T*)ctx->tout_b, 1},
                                  st, F_DEN_TIME_MODS)));
     TRY((gemm_w<T, false, false>(ctx, cond + (size_t)m0 * W1, W1, (const T*)ctx->mod_w,
-                                 (const T*)ctx->mod_w_p, mm, nmod, W1,
+                                 (const T*)ctx->mod_w_p, ctx->mod_w_q, mm, nmod, W1,
                                  EpiStore<T>{(T*)ctx->mods + (size_t)m0 * nmod, nmod,
                                              (const T*)ctx->mod_b, 0},
                                  st, F_DEN_TIME_MODS)));
@@ -772,7 +786,7 @@ int run_suffix(pi0_ctx* ctx, int B, const float* keys, const T* values, const vo
       eq.q16 = (T*)ctx->q16s;
       eq.k16 = (T*)ctx->ksuf16;
     }
-    TRY((gemm_w<T, true, false>(ctx, x, W1, (const T*)w.qkv, (const T*)w.qkv_p, M, hq + 2 * hkv,
+    TRY((gemm_w<T, true, false>(ctx, x, W1, (const T*)w.qkv, (const T*)w.qkv_p, w.qkv_q, M, hq + 2 * hkv,
                                 W1, eq, st, F_DEN_QKV, m_in, xn)));
     bool done_attn = false;
     if constexpr (!Tr<T>::kBf16) {
@@ -801,11 +815,11 @@ int run_suffix(pi0_ctx* ctx, int B, const float* keys, const T* values, const vo
     a.a_is_ready = 1;  // the prefix K/V cache comes from prefill, not from this step
     TRY(attn_launch<T>(ctx, a, B, true, st, F_DEN_ATTN));
     }
-    TRY((gemm_w<T, false, true>(ctx, attn, hq, (const T*)w.o, (const T*)w.o_p, M, W1, hq,
+    TRY((gemm_w<T, false, true>(ctx, attn, hq, (const T*)w.o, (const T*)w.o_p, w.o_q, M, W1, hq,
                                 EpiGatedResid<T>{x, W1, m_in + 2 * W1, M, 0}, st, F_DEN_O)));
-    TRY((gemm_w<T, true, false>(ctx, x, W1, (const T*)w.gu, (const T*)w.gu_p, M, 2 * F1, W1,
+    TRY((gemm_w<T, true, false>(ctx, x, W1, (const T*)w.gu, (const T*)w.gu_p, w.gu_q, M, 2 * F1, W1,
                                 EpiGeglu<T>{h, F1}, st, F_DEN_GU, m_post, xn)));
-    TRY((gemm_w<T, false, true>(ctx, h, F1, (const T*)w.d, (const T*)w.d_p, M, W1, F1,
+    TRY((gemm_w<T, false, true>(ctx, h, F1, (const T*)w.d, (const T*)w.d_p, w.d_q, M, W1, F1,
                                 EpiGatedResid<T>{x, W1, m_post + 2 * W1, M, 0}, st, F_DEN_DOWN)));
   }
   {
@@ -864,7 +878,9 @@ int attr_tc(pi0_ctx* ctx) {
 }
 template <typename T, int NA, class Epi, bool SSQ = false>
 int attr_sk(pi0_ctx* ctx) {
-  for (auto k : {sk::skinny_kernel<T, NA, false, SSQ, Epi>, sk::skinny_kernel<T, NA, !SSQ, SSQ, Epi>}) {
+  for (auto k : {sk::skinny_kernel<T, NA, false, SSQ, Epi>, sk::skinny_kernel<T, NA, !SSQ, SSQ, Epi>,
+                 sk::skinny_kernel<T, NA, false, SSQ, Epi, 4>, sk::skinny_kernel<T, NA, !SSQ, SSQ, Epi, 4>,
+                 sk::skinny_kernel<T, NA, false, SSQ, Epi, 3>, sk::skinny_kernel<T, NA, !SSQ, SSQ, Epi, 3>}) {
     CK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, sk::SkSmem<NA>::BYTES));
     CK(cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
   }
@@ -984,6 +1000,20 @@ int alloc_all(pi0_ctx* ctx) {
   };
   arena += L * (packed(hq + 2 * hkv, W1) + packed(W1, hq) + packed(2 * F1, W1) + packed(W1, F1)) +
            packed(nmodw, W1) + 2 * packed(W1, W1);
+  // quantised models whose action-expert dimensions are whole 64-wide k-blocks: the same
+  // matrices as group-quantised blocks, dequantised inside the weight-streaming kernel
+  ctx->qb = 0;
+  if (e == 2 && W1 % 64 == 0 && hq % 64 == 0 && F1 % 64 == 0)
+    ctx->qb = g.quant == PI0_QUANT_Q4 ? 4 : g.quant == PI0_QUANT_Q3 ? 3 : 0;
+  auto qpacked = [&](size_t n, size_t k) {
+    return ((n + 127) / 128) * ((k + 63) / 64) * (size_t)sk::qw_block(ctx->qb);
+  };
+  const size_t qbytes =
+      ctx->qb ? L * (qpacked(hq + 2 * hkv, W1) + qpacked(W1, hq) + qpacked(2 * F1, W1) +
+                     qpacked(W1, F1)) +
+                    qpacked(nmodw, W1) + 2 * qpacked(W1, W1)
+              : 0;
+  arena += qbytes;
   ctx->arena_bytes = arena;
   TRY(dev_alloc(ctx, &ctx->arena, ctx->arena_bytes));
   char* p = (char*)ctx->arena;
@@ -1034,6 +1064,20 @@ int alloc_all(pi0_ctx* ctx) {
   ctx->mod_w_p = take_bytes(packed(nmodw, W1));
   ctx->tin_p = take_bytes(packed(W1, W1));
   ctx->tout_p = take_bytes(packed(W1, W1));
+  if (ctx->qb) {
+    char* q0 = p;
+    for (int l = 0; l < L; ++l) {
+      LayerW& w = ctx->suf[l];
+      w.qkv_q = take_bytes(qpacked(hq + 2 * hkv, W1));
+      w.o_q = take_bytes(qpacked(W1, hq));
+      w.gu_q = take_bytes(qpacked(2 * F1, W1));
+      w.d_q = take_bytes(qpacked(W1, F1));
+    }
+    ctx->mod_w_q = take_bytes(qpacked(nmodw, W1));
+    ctx->tin_q = take_bytes(qpacked(W1, W1));
+    ctx->tout_q = take_bytes(qpacked(W1, W1));
+    CK(cudaMemset(q0, 0, (size_t)(p - q0)));  // rows past a matrix: zero codes and scales
+  }
   if ((size_t)(p - (char*)ctx->arena) > ctx->arena_bytes)
     return fail(ctx, PI0_ERR_INVALID, "internal: weight arena overflow");
 
@@ -1120,6 +1164,52 @@ int dequant_into(pi0_ctx* ctx, int quant, const uint32_t* qw, const T* scale, in
   return 0;
 }
 
+// Quantised Linear -> the group-quantised blocks of the weight-streaming GEMMs (action expert,
+// modulations, time MLP), with the same row re-layout (RoPE / gate-up permutations, fused row
+// offsets) as the 16-bit copies. Other Linears are left to the dequantised path.
+int pack_quantised(pi0_ctx* ctx, const Entry& en, const uint32_t* qw, const void* scale,
+                   cudaStream_t st) {
+  if (!qw) return fail(ctx, PI0_ERR_INVALID, "q_scale without its q_weight");
+  const pi0_config& g = ctx->cfg;
+  const int hq = g.num_heads * g.head_dim, hkv = g.num_kv_heads * g.head_dim;
+  const int W1 = g.ae_width, F1 = g.ae_mlp_dim;
+  void* dst = nullptr;
+  const int* idx = nullptr;
+  int row0 = 0;
+  if (en.role <= R_D && en.expert == 1) {
+    const LayerW& w = ctx->suf[en.layer];
+    switch (en.role) {
+      case R_Q: dst = w.qkv_q; idx = ctx->perm_q; break;
+      case R_K: dst = w.qkv_q; idx = ctx->perm_k; row0 = hq; break;
+      case R_V: dst = w.qkv_q; row0 = hq + hkv; break;
+      case R_O: dst = w.o_q; break;
+      case R_GU: dst = w.gu_q; idx = ctx->perm_gu1; break;
+      case R_D: dst = w.d_q; break;
+      default: break;
+    }
+  } else if (en.role == R_MOD_W) {
+    dst = ctx->mod_w_q;
+    row0 = en.layer * 3 * W1;
+  } else if (en.role == R_TIN_W) {
+    dst = ctx->tin_q;
+  } else if (en.role == R_TOUT_W) {
+    dst = ctx->tout_q;
+  }
+  if (!dst) return 0;
+  const int n = (int)en.shape[0], K = (int)en.in_dim, nkb = K / 64;
+  if (K % 64 || (K != W1 && K != hq && K != F1))
+    return fail(ctx, PI0_ERR_INVALID, "internal: quantised block layout for " + en.name);
+  const int threads = n * nkb;
+  if (ctx->qb == 4)
+    sk::pack_q_kernel<4><<<(threads + 255) / 256, 256, 0, st>>>(
+        (uint8_t*)dst, qw, (const uint16_t*)scale, idx, n, K, row0, nkb);
+  else
+    sk::pack_q_kernel<3><<<(threads + 255) / 256, 256, 0, st>>>(
+        (uint8_t*)dst, qw, (const uint16_t*)scale, idx, n, K, row0, nkb);
+  CKL();
+  return 0;
+}
+
 template <typename T>
 int set_params_impl(pi0_ctx* ctx, const void* const* params, cudaStream_t st) {
   const pi0_config& g = ctx->cfg;
@@ -1138,6 +1228,7 @@ int set_params_impl(pi0_ctx* ctx, const void* const* params, cudaStream_t st) {
       qw = static_cast<const uint32_t*>(src);
       continue;
     }
+    if (en.in_dim > 0 && ctx->qb) TRY(pack_quantised(ctx, en, qw, src, st));
     if (en.in_dim > 0) {
       // quantised Linear: w = (code − max_int)·scale in the model dtype, then the same re-layout
       // as an unquantised weight
@@ -1347,13 +1438,17 @@ int pi0_denoise_step_kv(pi0_ctx* ctx, int batch, const float* keys, const void* 
   TRY(check_ready(ctx, batch));
   if (!keys || !values || !x_t || !time_emb || !suffix_cos || !suffix_sin || !prefix_mask || !v_out)
     return fail(ctx, PI0_ERR_INVALID, "null tensor argument");
-  if (is_bf16(ctx))
-    return run_step<__nv_bfloat16>(ctx, batch, keys, (const __nv_bfloat16*)values,
-                                   (const __nv_bfloat16*)x_t, (const __nv_bfloat16*)time_emb,
-                                   suffix_cos, suffix_sin, prefix_mask, v_out, stream);
-  return run_step<__half>(ctx, batch, keys, (const __half*)values, (const __half*)x_t,
-                          (const __half*)time_emb, suffix_cos, suffix_sin, prefix_mask, v_out,
-                          stream);
+  auto body = [&](cudaStream_t st) {
+    if (is_bf16(ctx))
+      return run_step<__nv_bfloat16>(ctx, batch, keys, (const __nv_bfloat16*)values,
+                                     (const __nv_bfloat16*)x_t, (const __nv_bfloat16*)time_emb,
+                                     suffix_cos, suffix_sin, prefix_mask, v_out, st);
+    return run_step<__half>(ctx, batch, keys, (const __half*)values, (const __half*)x_t,
+                            (const __half*)time_emb, suffix_cos, suffix_sin, prefix_mask, v_out,
+                            st);
+  };
+  if (ctx->prof_on) return run_profiled(ctx, stream, body);
+  return body(stream);
 }
 
 int pi0_denoise_loop_kv(pi0_ctx* ctx, int batch, const float* keys, const void* values,
