@@ -24,6 +24,7 @@ bounded sample per step, and prints the same line with ``"impl": "reference"``.
 from __future__ import annotations
 
 import argparse
+import dataclasses
 import json
 import os
 import subprocess
@@ -484,6 +485,9 @@ def run_part(args):
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     cfg = full_config()
+    if args.layers == 2:  # profiling aid: every width of the full model, two layers
+        cfg = dataclasses.replace(cfg, paligemma_variant="gemma_2b_2l",
+                                  action_expert_variant="gemma_300m_2l")
     if args.quant != "none":
         from mlc_vla.quant import PRESETS
 
@@ -531,7 +535,8 @@ def run_part(args):
     torch.cuda.synchronize(dev)
     ms = e0.elapsed_time(e1) / max(1, args.steps)
     print(json.dumps({"part": args.part, "ms": ms, "steps": args.steps, "warmup": args.warmup,
-                      "config": f"pi0.5 fp16 batch 1 (full size), weights {args.quant}",
+                      "config": f"pi0.5 fp16 batch 1 (full widths, {cfg.vlm.depth} layers), "
+                                f"weights {args.quant}",
                       "families_ms": {k: round(v[1], 4) for k, v in sorted(
                           fam.items(), key=lambda kv: -kv[1][1])}}),
           flush=True)
@@ -554,6 +559,8 @@ def main():
                     help="profiling aid: time only the prefill or one denoise step")
     ap.add_argument("--quant", default="none", choices=["none", "q4f16_1", "q3f16_1"],
                     help="with --part: group-quantised weights (fused dequant in the denoise GEMMs)")
+    ap.add_argument("--layers", type=int, default=18, choices=[2, 18],
+                    help="with --part: 2 = full widths with two layers, for small profiler captures")
     args = ap.parse_args()
     if args.part != "chunk":
         return run_part(args)
