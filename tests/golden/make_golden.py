@@ -22,6 +22,10 @@ What it does:
    ≥ 0.99999 here before the fixture is written.
 4. Writes the dtype-faithful fp16 oracle outputs of the ``mini`` configuration, which the
    GPU tests compare against.
+5. Writes ``loader_map.json``: the reference loader's complete name map (``build_name_map``:
+   target name -> source keys and the transform's name) for the ``mini`` and the full π0.5
+   configuration, the pin of this package's checkpoint loader. ``--loader-map-only`` writes
+   just this file.
 """
 
 from __future__ import annotations
@@ -101,14 +105,37 @@ def to_openpi_state_dict(ref, config, params):
     return {k: torch.from_numpy(np.ascontiguousarray(v, np.float32)) for k, v in sd.items()}
 
 
+def write_loader_map(ref):
+    """The reference loader's name map for the mini and the full configuration, as JSON (the
+    map reads only the depth, the vision depth and the π0.5 flag of the configuration it gets)."""
+    import json
+
+    from mlc_vla.model.pi0 import Pi0Config
+    from tests.golden import recipes
+
+    maps = {}
+    for label, kw in (("mini", recipes.MINI), ("full", recipes.FULL)):
+        config = Pi0Config(**kw)
+        maps[label] = {name: {"keys": list(spec.keys), "fn": spec.fn.__name__}
+                       for name, spec in ref.loader.build_name_map(config).items()}
+    path = os.path.join(HERE, "loader_map.json")
+    with open(path, "w") as f:
+        json.dump(maps, f, indent=0, sort_keys=True)
+    print("wrote", path, {k: len(v) for k, v in maps.items()})
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("MLC_VLA_REFERENCE", "/root/reference"))
+    ap.add_argument("--loader-map-only", action="store_true")
     args = ap.parse_args()
 
     ref = load_reference(args.reference)
     sys.path.insert(0, os.path.join(REPO, "mlc-vla_b200"))
     sys.path.insert(0, REPO)
+    write_loader_map(ref)
+    if args.loader_map_only:
+        return
     from mlc_vla.model.pi0 import Pi0Config
     from mlc_vla.model.pi0.pi0_model import backbone_named_params
     from oracle import pi0_oracle as O
