@@ -124,7 +124,8 @@ int pi0_dequantize_weight(int quant, int dtype, const uint32_t* q_weight, const 
 /* y[M, N] = x[M, K] · w[N, K]^T in the context's model dtype (fp32 accumulation, one rounding):
  * the GEMM engine every projection of the path runs on, exposed for direct tests. engine: 0 =
  * automatic, 1 = tcgen05 tiles (M >= 128), 2 = warp-level mma, 3 = tcgen05 weight-streaming
- * split-K (M <= 128). */
+ * split-K (M <= 128), 4 = tcgen05 128×256 tiles split over K between two CTAs of a cluster
+ * (M >= 128, K > 64). */
 int pi0_linear(pi0_ctx* ctx, const void* x, int M, int K, const void* w, int N, void* y,
                int engine, pi0_stream_t stream);
 

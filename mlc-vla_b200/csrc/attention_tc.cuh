@@ -30,10 +30,6 @@ namespace pi0 {
 namespace atc {
 
 using namespace tc;
-using sk::cluster_rank;
-using sk::cluster_sync;
-using sk::ld_cluster4;
-using sk::map_rank;
 using sk::workers_sync;
 
 constexpr int KB = 64;             // keys per tile

@@ -148,6 +148,31 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// ---- thread-block clusters: rank, barrier, distributed shared memory ----
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
+}
+// the address of this CTA's shared-memory location `saddr` in the CTA of cluster rank `rank`
+__device__ __forceinline__ uint32_t map_rank(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ float4 ld_cluster4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+
 template <int BN, int STAGES>
 struct Smem {
   static constexpr int A_BYTES = BM * BK * 2;
@@ -159,22 +184,33 @@ struct Smem {
                                         : 2 * BN <= 256 ? 256 : 512;
 };
 
-template <typename T, int BN, int STAGES, class Epi>
+// KS = 2: split-K over a cluster of two CTAs, one output tile per cluster (grid = 2·tiles, at
+// most one wave). Rank r accumulates k-blocks [r·⌈nk/2⌉, (r+1)·⌈nk/2⌉) and finishes output
+// columns [r·BN/2, (r+1)·BN/2): it parks the other half of its accumulator in its drained ring,
+// and after a cluster barrier adds the peer's parked half to its own through distributed shared
+// memory (p0 + p1, the same sum on both ranks) before the epilogue.
+template <typename T, int BN, int STAGES, class Epi, int KS = 1>
 __global__ void __launch_bounds__(192, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    int M, int N, int K, Epi epi, int* err) {
   using S = Smem<BN, STAGES>;
   static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN");
+  static_assert(KS == 1 || (KS == 2 && BN % 64 == 0 && 128 * (BN / 2 + 4) * 4 <= STAGES * S::STAGE),
+                "split-K pair: parked half must fit the ring");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sbase = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                               ~static_cast<uintptr_t>(1023));
   __shared__ __align__(8) uint64_t full[STAGES], empty[STAGES], tfull[2], tempty[2], drain;
   __shared__ uint32_t s_tmem;
+  bool epi_ok = false;  // KS > 1, epilogue warps: this CTA's accumulator is complete
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int m_tiles = (M + BM - 1) / BM, n_tiles = (N + BN - 1) / BN;
   const int tiles = m_tiles * n_tiles;
-  const int nk = (K + BK - 1) / BK;
+  const uint32_t rank = KS > 1 ? cluster_rank() : 0;
+  const int nk_all = (K + BK - 1) / BK, kper = (nk_all + KS - 1) / KS;
+  const int kb0 = (int)rank * kper, nk = max(0, min(nk_all, kb0 + kper) - kb0);
+  const int t_first = blockIdx.x / KS, t_step = gridDim.x / KS;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -209,14 +245,14 @@ __global__ void __launch_bounds__(192, 1)
       uint32_t ph = 0;
       uint32_t issued = 0;  // bit s: stage s has a load in flight or landed (phase ph_of[s])
       uint32_t ph_of = 0;
-      for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+      for (int t = t_first; t < tiles; t += t_step) {
         const int m0 = (t % m_tiles) * BM, n0 = (t / m_tiles) * BN;
         for (int kb = 0; kb < nk; ++kb) {
           if (!mbar_wait(&empty[s], ph ^ 1, err, ERR_TIMEOUT_PRODUCER)) goto producer_done;
           uint8_t* st = sbase + s * S::STAGE;
           mbar_expect_tx(&full[s], S::STAGE);
-          tma_load_2d(st, &tmA, &full[s], kb * BK, m0);
-          tma_load_2d(st + S::A_BYTES, &tmB, &full[s], kb * BK, n0);
+          tma_load_2d(st, &tmA, &full[s], (kb0 + kb) * BK, m0);
+          tma_load_2d(st + S::A_BYTES, &tmB, &full[s], (kb0 + kb) * BK, n0);
           issued |= 1u << s;
           ph_of = (ph_of & ~(1u << s)) | (ph << s);
           if (++s == STAGES) {
@@ -237,7 +273,7 @@ __global__ void __launch_bounds__(192, 1)
       int s = 0;
       uint32_t ph = 0;
       int i = 0;
-      for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++i) {
+      for (int t = t_first; t < tiles; t += t_step, ++i) {
         const int acc = i & 1;
         const uint32_t aph = (i >> 1) & 1;
         if (!mbar_wait(&tempty[acc], aph ^ 1, err, ERR_TIMEOUT_MMA)) break;
@@ -264,10 +300,32 @@ __global__ void __launch_bounds__(192, 1)
       umma_commit(&drain);
       mbar_wait(&drain, 0, err, ERR_TIMEOUT_MMA, false);
     }
+  } else if (KS > 1) {  // split-K pair: park the peer's half of the accumulator
+    const int q = warp & 3;
+    bool ok = t_first < tiles && nk > 0;
+    if (ok && lane == 0) ok = mbar_wait(&tfull[0], 0, err, ERR_TIMEOUT_EPI);
+    ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+    epi_ok = ok;
+    if (ok) {
+      tc_fence_after();
+      constexpr int H = BN / 2, XLD = H + 4;
+      float* park = reinterpret_cast<float*>(sbase) + (q * 32 + lane) * XLD;
+      const int pc0 = (1 - (int)rank) * H;
+#pragma unroll 1
+      for (int c = 0; c < H; c += 32) {
+        uint32_t v[32];
+        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + pc0 + c, v);
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          *reinterpret_cast<float4*>(park + c + 4 * u) =
+              make_float4(__uint_as_float(v[4 * u]), __uint_as_float(v[4 * u + 1]),
+                          __uint_as_float(v[4 * u + 2]), __uint_as_float(v[4 * u + 3]));
+      }
+    }
   } else {  // epilogue warps 2..5: TMEM lane quarter = warp % 4
     const int q = warp & 3;
     int i = 0;
-    for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++i) {
+    for (int t = t_first; t < tiles; t += t_step, ++i) {
       const int acc = i & 1;
       const uint32_t aph = (i >> 1) & 1;
       const int m0 = (t % m_tiles) * BM, n0 = (t / m_tiles) * BN;
@@ -301,6 +359,50 @@ __global__ void __launch_bounds__(192, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
     }
+  }
+
+  if constexpr (KS > 1) {
+    // every rank's half is parked: add the peer's half of this rank's columns and finish them
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();
+    if (warp >= 2 && epi_ok) {
+      tc_fence_after();
+      constexpr int H = BN / 2, XLD = H + 4;
+      const int q = warp & 3, t = t_first;
+      const int m0 = (t % m_tiles) * BM, n0 = (t / m_tiles) * BN + (int)rank * H;
+      const int row = m0 + q * 32 + lane;
+      const uint32_t peer = map_rank(
+          smem_u32(reinterpret_cast<float*>(sbase) + (q * 32 + lane) * XLD), 1u - rank);
+      if (row < M) epi.prefetch(row, n0);
+#pragma unroll 1
+      for (int c = 0; c < H; c += 32) {
+        uint32_t v[32];
+        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (int)rank * H + c, v);
+        float4 pv[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) pv[u] = ld_cluster4(peer + (uint32_t)(c + 4 * u) * 4u);
+        float vf[32];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          vf[4 * u] = __uint_as_float(v[4 * u]) + pv[u].x;
+          vf[4 * u + 1] = __uint_as_float(v[4 * u + 1]) + pv[u].y;
+          vf[4 * u + 2] = __uint_as_float(v[4 * u + 2]) + pv[u].z;
+          vf[4 * u + 3] = __uint_as_float(v[4 * u + 3]) + pv[u].w;
+        }
+        if (row < M) {
+          if (c + 32 < H && n0 + c + 32 < N) epi.prefetch(row, n0 + c + 32);
+          if (!(n0 + c + 32 <= N && epi.chunk32(row, n0 + c, vf))) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const int col = n0 + c + 2 * j;
+              if (col < N) epi(row, col, vf[2 * j], vf[2 * j + 1]);
+            }
+          }
+        }
+      }
+    }
+    cluster_sync();  // the peer may still be reading this CTA's parked half
   }
 
   tc_fence_before();

@@ -379,6 +379,29 @@ int gemm_tc_launch(pi0_ctx* ctx, const T* A, int lda, const T* W, int ldw, int M
                 tc::Smem<BN, ST>::BYTES, st, dim3(1, 1, 1), ta, tb, M, N, K, epi, ctx->dev_err);
 }
 
+// Split-K pair (gemm_tc_kernel KS = 2) with 128×256 tiles: for a GEMM whose 256-wide tiles fill
+// under half the SMs but whose K is long (the prefill down projection: 64 tiles, K = 16384), two
+// CTAs per tile keep every SM's tensor pipe fed from a 4-stage ring of 256-wide stages, which a
+// 128-wide tile's ring of the same size cannot (its stages drain faster than L2 refills them).
+bool use_splitk_pair(int M, int N, int K, int sms) {
+  const int tiles = ((M + tc::BM - 1) / tc::BM) * ((N + 255) / 256);
+  return K >= 64 * tc::BK && 2 * tiles <= sms && 4 * tiles > sms;
+}
+template <typename T, class Epi>
+int gemm_tc_pair_launch(pi0_ctx* ctx, const T* A, int lda, const T* W, int ldw, int M, int N,
+                        int K, const Epi& epi, cudaStream_t st, int fam) {
+  CUtensorMap ta, tb;
+  const bool bf = Tr<T>::kBf16;
+  TRY(make_tmap(ctx, &ta, A, M, K, lda, tc::BM, bf));
+  TRY(make_tmap(ctx, &tb, W, N, K, ldw, 256, bf));
+  const int tiles = ((M + tc::BM - 1) / tc::BM) * ((N + 255) / 256);
+  if ((K + tc::BK - 1) / tc::BK < 2)
+    return fail(ctx, PI0_ERR_UNSUPPORTED, "split-K pair: K must span at least two k-blocks");
+  Prof pr(ctx, fam, st);
+  return launch(ctx, tc::gemm_tc_kernel<T, 256, 4, Epi, 2>, dim3(2 * tiles), dim3(192),
+                tc::Smem<256, 4>::BYTES, st, dim3(2, 1, 1), ta, tb, M, N, K, epi, ctx->dev_err);
+}
+
 template <typename T>
 int rmsnorm(pi0_ctx* ctx, const T* x, T* out, int rows, int W, const T* w, const T* mod,
             int rows_per_mod, int mod_stride, cudaStream_t st, int fam);
@@ -511,7 +534,9 @@ int gemm(pi0_ctx* ctx, const T* A, int lda, const T* W, int ldw, int M, int N, i
     if (M <= 64) return skinny_launch<T, 64, false, false>(ctx, A, lda, W, ldw, M, N, K, epi, st, fam, SkOpt{});
     return skinny_launch<T, 128, false, false>(ctx, A, lda, W, ldw, M, N, K, epi, st, fam, SkOpt{});
   }
-  if ((engine == 0 && M >= 128 && ctx->use_tc) || engine == 1) {
+  if ((engine == 0 && M >= 128 && ctx->use_tc) || engine == 1 || engine == 4) {
+    if (engine == 4 || (engine == 0 && use_splitk_pair(M, N, K, ctx->num_sms)))
+      return gemm_tc_pair_launch<T>(ctx, A, lda, W, ldw, M, N, K, epi, st, fam);
     switch (pick_bn(M, N, ctx->num_sms)) {
       case 256: return gemm_tc_launch<T, 256, 4>(ctx, A, lda, W, ldw, M, N, K, epi, st, fam);
       case 160: return gemm_tc_launch<T, 160, 5>(ctx, A, lda, W, ldw, M, N, K, epi, st, fam);
@@ -870,9 +895,9 @@ int attr_gemm(pi0_ctx* ctx) {
                           GemmCfg<T, BM, BN, WM, WN, ST>::SMEM));
   return 0;
 }
-template <typename T, int BN, int ST, class Epi>
+template <typename T, int BN, int ST, class Epi, int KS = 1>
 int attr_tc(pi0_ctx* ctx) {
-  CK(cudaFuncSetAttribute(tc::gemm_tc_kernel<T, BN, ST, Epi>,
+  CK(cudaFuncSetAttribute(tc::gemm_tc_kernel<T, BN, ST, Epi, KS>,
                           cudaFuncAttributeMaxDynamicSharedMemorySize, tc::Smem<BN, ST>::BYTES));
   return 0;
 }
@@ -893,6 +918,7 @@ int attr_gemm_both(pi0_ctx* ctx) {
   TRY((attr_gemm<T, 128, 128, 64, 32, 4, Epi>(ctx)));
   TRY((attr_gemm<T, 64, 64, 32, 32, 4, Epi>(ctx)));
   TRY((attr_tc<T, 256, 4, Epi>(ctx)));
+  TRY((attr_tc<T, 256, 4, Epi, 2>(ctx)));
   TRY((attr_tc<T, 160, 5, Epi>(ctx)));
   TRY((attr_tc<T, 128, 6, Epi>(ctx)));
   return 0;

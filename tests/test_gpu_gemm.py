@@ -16,7 +16,7 @@ def rt():
     return Pi0Runtime(config(recipes.MINI), device=0)
 
 
-@pytest.mark.parametrize("engine", [1, 2, 3])
+@pytest.mark.parametrize("engine", [1, 2, 3, 4])
 @pytest.mark.parametrize("m,n,k", [(128, 256, 64), (968, 2560, 2048), (200, 160, 320),
                                    (50, 1024, 4096), (777, 390, 96), (1000, 32768, 128),
                                    (50, 2560, 1024), (50, 8192, 1024), (50, 1024, 2048),
@@ -29,6 +29,8 @@ def test_linear_matches_torch_fp32(rt, engine, m, n, k):
         pytest.skip("weight-streaming engine: M <= 128, K <= 4096")
     if engine == 1 and m < 128:
         pytest.skip("tile engine: M >= 128")
+    if engine == 4 and (m < 128 or k <= 64):
+        pytest.skip("split-K pair engine: M >= 128, K > 64")
     g = torch.Generator(device="cuda").manual_seed(m * 7 + n + k)
     x = torch.randn((m, k), generator=g, device="cuda").half()
     w = (0.05 * torch.randn((n, k), generator=g, device="cuda")).half()
