@@ -20,8 +20,9 @@
 //   * O += P·V: tcgen05.mma kind::f16, M=128, N=hd, K=64, V read MN-major straight from its
 //     cache layout ([keys, hd], hd contiguous), fp32 accumulator in TMEM (hd columns).
 //   * final O / l (or, with key splits, the (m, l, O) partials merged across the cluster).
-// Warp roles: warp 0 TMA producer (Q once, K/V tiles through a 2-stage ring; cached prefix tiles
-// are requested before griddepcontrol.wait), warp 1 MMA issuer, warps 2-5 softmax/epilogue.
+// Warp roles: warp 0 TMA producer (Q once; K and V tiles through separate 2-slot rings, a K slot
+// refilled once its S MMA is done and a V slot once its P·V is done; cached prefix tiles are
+// requested before griddepcontrol.wait), warp 1 MMA issuer, warps 2-5 softmax/epilogue.
 // All waits are bounded (gemm_tc.cuh: mbar_wait).
 #pragma once
 
@@ -88,6 +89,58 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       : "memory");
 }
 
+// Final rows [rbeg, rend) of a row tile from the nsplit ≤ NSB key-split partials (unnormalised O
+// at `oaddr` in every rank's shared memory, row stride OLD floats; merge weights s_w, 1 / Σ w·l in
+// s_inv): one item = (row, 4 dims); a thread takes G = 32 / NSB items per pass and issues the
+// G·nsplit cluster loads of all of them together, so a pass costs one round trip over the
+// cluster. The partials of an item are summed in rank order.
+template <int HD, int NSB>
+__device__ __forceinline__ void merge_rows(const AtcArgs& a, int b, int row0, int rbeg, int rend,
+                                           int nsplit, uint32_t oaddr, float (*s_w)[16],
+                                           const float* s_inv, int tid) {
+  constexpr int G = 32 / NSB, OLD = AtcSmem<HD>::OLD;
+  const int items = (rend - rbeg) * (HD / 4);
+#pragma unroll 1
+  for (int it0 = tid; it0 < items; it0 += G * NT) {
+    float4 v[G][NSB];
+#pragma unroll
+    for (int j = 0; j < G; ++j) {
+      const int it = it0 + j * NT;
+      if (it < items) {
+        const int rr = it / (HD / 4), d = (it % (HD / 4)) * 4;
+        const uint32_t off = oaddr + ((rbeg + rr) * OLD + d) * 4;
+#pragma unroll
+        for (int c = 0; c < NSB; ++c)
+          if (c < nsplit) v[j][c] = ld_cluster4(map_rank(off, c));
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < G; ++j) {
+      const int it = it0 + j * NT;
+      if (it < items) {
+        const int rr = it / (HD / 4), d = (it % (HD / 4)) * 4;
+        const int row = row0 + rbeg + rr;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int c = 0; c < NSB; ++c)
+          if (c < nsplit) {
+            const float w = s_w[rr][c];
+            acc.x += w * v[j][c].x;
+            acc.y += w * v[j][c].y;
+            acc.z += w * v[j][c].z;
+            acc.w += w * v[j][c].w;
+          }
+        if (row < a.rows) {
+          const float inv = s_inv[rr];
+          __half* out = reinterpret_cast<__half*>(a.out) + ((size_t)b * a.rows + row) * HD + d;
+          *reinterpret_cast<uint2*>(out) = make_uint2(Tr<__half>::pack(acc.x * inv, acc.y * inv),
+                                                      Tr<__half>::pack(acc.z * inv, acc.w * inv));
+        }
+      }
+    }
+  }
+}
+
 template <int HD>
 __global__ void __launch_bounds__(NT, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKA,
@@ -98,8 +151,10 @@ __global__ void __launch_bounds__(NT, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
-  __shared__ __align__(8) uint64_t q_full, kv_full[2], kv_empty[2], s_full, s_free, p_full,
-      pv_done, drain;
+  // K and V tiles travel in separate two-slot rings: a K slot is free once its S = Q·Kᵀ is done,
+  // a V slot once its O += P·V is done, so the next K tiles do not wait for the P·V chain
+  __shared__ __align__(8) uint64_t q_full, k_full[2], k_empty[2], v_full[2], v_empty[2], s_full,
+      s_free, p_full, pv_done, drain;
   __shared__ uint32_t s_tmem;
   __shared__ float s_mask[KB];
   __shared__ float s_w[128][16];
@@ -120,8 +175,10 @@ __global__ void __launch_bounds__(NT, 1)
   if (tid == 0) {
     mbar_init(&q_full, 1);
     for (int s = 0; s < 2; ++s) {
-      mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
     }
     mbar_init(&s_full, 1);
     mbar_init(&s_free, 4);
@@ -144,24 +201,26 @@ __global__ void __launch_bounds__(NT, 1)
   tc_fence_after();
   const uint32_t tmem = s_tmem;  // S: columns [0, 64); O: columns [256, 256 + HD)
 
-  auto issue_kv = [&](int i) {
+  // one K (is_v = false) or V tile of key tile i into ring slot i & 1
+  auto issue = [&](int i, bool is_v) {
     const int s = i & 1, tile = tbeg + i;
     const bool inA = tile < a.ntA;
-    const CUtensorMap* mk = inA ? &tmKA : &tmKB;
-    const CUtensorMap* mv = inA ? &tmVA : &tmVB;
+    const CUtensorMap* m = inA ? (is_v ? &tmVA : &tmKA) : (is_v ? &tmVB : &tmKB);
     const int y = inA ? b * a.LA + tile * KB : b * a.LB + (tile - a.ntA) * KB;
-    mbar_expect_tx(&kv_full[s], S::STAGE);
+    uint64_t* bar = is_v ? &v_full[s] : &k_full[s];
+    uint8_t* dst = is_v ? sV(s) : sK(s);
+    mbar_expect_tx(bar, is_v ? S::V_BYTES : S::K_BYTES);
 #pragma unroll
-    for (int kb = 0; kb < NKB; ++kb) {
-      tma_load_2d(sK(s) + kb * (KB * 128), mk, &kv_full[s], kb * 64, y);
-      tma_load_2d(sV(s) + kb * (KB * 128), mv, &kv_full[s], kb * 64, y);
-    }
+    for (int kb = 0; kb < NKB; ++kb) tma_load_2d(dst + kb * (KB * 128), m, bar, kb * 64, y);
   };
 
   // tiles of the cached prefix do not depend on the previous kernel
-  int issued = 0;
+  int issued = 0;  // K and V of tiles [0, issued) requested
   if (tid == 0 && a.a_ready)
-    while (issued < min(n, 2) && tbeg + issued < a.ntA) issue_kv(issued++);
+    for (; issued < min(n, 2) && tbeg + issued < a.ntA; ++issued) {
+      issue(issued, false);
+      issue(issued, true);
+    }
   pdl_trigger();
   pdl_wait();
 
@@ -171,16 +230,22 @@ __global__ void __launch_bounds__(NT, 1)
 #pragma unroll
       for (int kb = 0; kb < NKB; ++kb)
         tma_load_2d(sQ + kb * (128 * 128), &tmQ, &q_full, kb * 64, b * a.rows + row0);
+      int issued_k = issued;  // K of tiles [0, issued_k) requested; V of [0, issued)
       for (int i = issued; i < n; ++i) {
-        if (i >= 2 && !mbar_wait(&kv_empty[i & 1], ((i >> 1) - 1) & 1, a.err, ERR_TIMEOUT_PRODUCER))
-          break;
-        issue_kv(i);
+        const uint32_t ph = ((i >> 1) - 1) & 1;
+        if (i >= 2 && !mbar_wait(&k_empty[i & 1], ph, a.err, ERR_TIMEOUT_PRODUCER)) break;
+        issue(i, false);
+        issued_k = i + 1;
+        if (i >= 2 && !mbar_wait(&v_empty[i & 1], ph, a.err, ERR_TIMEOUT_PRODUCER)) break;
+        issue(i, true);
         issued = i + 1;
       }
       // no copy into this CTA's shared memory may still be in flight when it exits
       mbar_wait(&q_full, 0, a.err, ERR_TIMEOUT_PRODUCER, false);
+      for (int i = max(0, issued_k - 2); i < issued_k; ++i)
+        mbar_wait(&k_full[i & 1], (i >> 1) & 1, a.err, ERR_TIMEOUT_PRODUCER, false);
       for (int i = max(0, issued - 2); i < issued; ++i)
-        mbar_wait(&kv_full[i & 1], (i >> 1) & 1, a.err, ERR_TIMEOUT_PRODUCER, false);
+        mbar_wait(&v_full[i & 1], (i >> 1) & 1, a.err, ERR_TIMEOUT_PRODUCER, false);
     }
   } else if (warp == 1) {
     if (lane == 0 && n > 0) {  // MMA issuer
@@ -189,7 +254,7 @@ __global__ void __launch_bounds__(NT, 1)
       bool ok = mbar_wait(&q_full, 0, a.err, ERR_TIMEOUT_MMA);
       auto qk = [&](int i) -> bool {
         const int s = i & 1;
-        if (!mbar_wait(&kv_full[s], (i >> 1) & 1, a.err, ERR_TIMEOUT_MMA)) return false;
+        if (!mbar_wait(&k_full[s], (i >> 1) & 1, a.err, ERR_TIMEOUT_MMA)) return false;
         tc_fence_after();
 #pragma unroll
         for (int kb = 0; kb < NKB; ++kb) {
@@ -199,18 +264,21 @@ __global__ void __launch_bounds__(NT, 1)
           for (int k = 0; k < 4; ++k) umma_f16(tmem, da + 2 * k, db + 2 * k, id_s, (kb | k) != 0);
         }
         umma_commit(&s_full);
+        umma_commit(&k_empty[s]);
         return true;
       };
       auto pv = [&](int i) -> bool {
         const int s = i & 1;
-        if (!mbar_wait(&p_full, i & 1, a.err, ERR_TIMEOUT_MMA)) return false;
+        if (!mbar_wait(&p_full, i & 1, a.err, ERR_TIMEOUT_MMA) ||
+            !mbar_wait(&v_full[s], (i >> 1) & 1, a.err, ERR_TIMEOUT_MMA))
+          return false;
         tc_fence_after();
         const uint64_t da = desc_sw128(smem_u32(sP));
         const uint64_t db = desc_sw128_mn(smem_u32(sV(s)), a.v_lbo, a.v_sbo);
 #pragma unroll
         for (int k = 0; k < 4; ++k)  // 16 keys (2048 bytes of V rows) per step
           umma_f16(tmem + 256, da + 2 * k, db + (uint64_t)(128 * k), id_o, (i | k) != 0);
-        umma_commit(&kv_empty[s]);
+        umma_commit(&v_empty[s]);
         umma_commit(&pv_done);
         return true;
       };
@@ -362,7 +430,7 @@ __global__ void __launch_bounds__(NT, 1)
     cluster_sync();
     const float* sO = reinterpret_cast<const float*>(base);
     const float* sML = sO + 128 * S::OLD;
-    const uint32_t oaddr = smem_u32(sO), maddr = smem_u32(sML);
+    const uint32_t maddr = smem_u32(sML);
     const int rpr = (128 + nsplit - 1) / nsplit;
     const int rbeg = rank * rpr, rend = min(128, rbeg + rpr);
     for (int rr = tid; rr < rend - rbeg; rr += NT) {
@@ -391,47 +459,9 @@ __global__ void __launch_bounds__(NT, 1)
       s_inv[rr] = L > 0.f ? 1.f / L : 0.f;
     }
     __syncthreads();
-    // one (row, 4 dims) item per thread and pass; the nsplit partials of an item are loaded
-    // together (static indices, predicated), then summed in rank order
-    const int items = (rend - rbeg) * (HD / 4);
-    // two items per pass, the 2·nsplit loads of both issued together: each pass costs one
-    // round trip over the cluster
-    auto finish = [&](int it, const float4 (&v)[16]) {
-      const int rr = it / (HD / 4), d = (it % (HD / 4)) * 4;
-      const int j = row0 + rbeg + rr;
-      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-      for (int c = 0; c < 16; ++c)
-        if (c < nsplit) {
-          const float w = s_w[rr][c];
-          acc.x += w * v[c].x;
-          acc.y += w * v[c].y;
-          acc.z += w * v[c].z;
-          acc.w += w * v[c].w;
-        }
-      if (j < a.rows) {
-        const float inv = s_inv[rr];
-        __half* out = reinterpret_cast<__half*>(a.out) + ((size_t)b * a.rows + j) * HD + d;
-        *reinterpret_cast<uint2*>(out) =
-            make_uint2(Tr<__half>::pack(acc.x * inv, acc.y * inv), Tr<__half>::pack(acc.z * inv, acc.w * inv));
-      }
-    };
-    auto load = [&](int it, float4 (&v)[16]) {
-      const int rr = it / (HD / 4), d = (it % (HD / 4)) * 4;
-      const uint32_t off = oaddr + ((rbeg + rr) * S::OLD + d) * 4;
-#pragma unroll
-      for (int c = 0; c < 16; ++c)
-        if (c < nsplit) v[c] = ld_cluster4(map_rank(off, c));
-    };
-#pragma unroll 1
-    for (int it = tid; it < items; it += 2 * NT) {
-      float4 v0[16], v1[16];
-      const bool two = it + NT < items;
-      load(it, v0);
-      if (two) load(it + NT, v1);
-      finish(it, v0);
-      if (two) finish(it + NT, v1);
-    }
+    if (nsplit <= 4) merge_rows<HD, 4>(a, b, row0, rbeg, rend, nsplit, smem_u32(sO), s_w, s_inv, tid);
+    else if (nsplit <= 8) merge_rows<HD, 8>(a, b, row0, rbeg, rend, nsplit, smem_u32(sO), s_w, s_inv, tid);
+    else merge_rows<HD, 16>(a, b, row0, rbeg, rend, nsplit, smem_u32(sO), s_w, s_inv, tid);
     cluster_sync();  // peers may still read this CTA's partial
   }
   tc_fence_before();
