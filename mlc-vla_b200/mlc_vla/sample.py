@@ -91,6 +91,9 @@ class PiZeroRunner:
         self.dev = self.ex.device
         self.vm = self.ex
         self._stage = {}
+        # device copies of tables derived from the inputs alone (pad mask + suffix RoPE per pad
+        # pattern, time embeddings per step count): computed and uploaded once, not per call
+        self._tables = {}
 
     def to_params(self, arrays):
         """Move numpy weights (ordered as ``named_params``) to the GPU."""
@@ -110,12 +113,31 @@ class PiZeroRunner:
         Returns (keys, values, prefix_mask, suffix_cos, suffix_sin, num_valid)."""
         cfg = self.config
         b = self._batch(prefix_embs)
-        hd = cfg.vlm.head_dim
         if prefix_pad is None:
             pads = [None] * b
         else:
             pp = np.asarray(prefix_pad).reshape(-1, cfg.prefix_len)
             pads = [pp[min(i, pp.shape[0] - 1)] for i in range(b)]
+        prefix_mask, suffix_cos, suffix_sin, nvs = self._pad_tables(pads)
+        dev = self.dev
+        x = prefix_embs if isinstance(prefix_embs, torch.Tensor) else np.asarray(prefix_embs)
+        prefix_dev = to_device(x, self._dt(), dev)
+        st = self._staging(b)
+        k, v = self.ex.prefill(prefix_dev, prefix_mask, params, keys=st["keys"], values=st["values"])
+        keys, values = DeviceArray(k), DeviceArray(v)
+        num_valid = nvs[0] if b == 1 else nvs
+        return keys, values, prefix_mask, suffix_cos, suffix_sin, num_valid
+
+    def _pad_tables(self, pads):
+        """(prefix mask, suffix cos, suffix sin) on the device and the valid counts for one
+        pad pattern per request (None = all valid), cached by the patterns' contents."""
+        key = ("pad",) + tuple(None if p is None else np.asarray(p, np.float32).tobytes()
+                               for p in pads)
+        hit = self._tables.get(key)
+        if hit is not None:
+            return hit
+        cfg = self.config
+        hd = cfg.vlm.head_dim
         masks, coss, sins, nvs = [], [], [], []
         for pad in pads:
             if pad is None:
@@ -130,16 +152,21 @@ class PiZeroRunner:
             sins.append(s)
             nvs.append(nv)
         dev = self.dev
-        prefix_mask = to_device(np.concatenate(masks, 0), "float32", dev)
-        suffix_cos = to_device(np.concatenate(coss, 0), "float32", dev)
-        suffix_sin = to_device(np.concatenate(sins, 0), "float32", dev)
-        x = prefix_embs if isinstance(prefix_embs, torch.Tensor) else np.asarray(prefix_embs)
-        prefix_dev = to_device(x, self._dt(), dev)
-        st = self._staging(b)
-        k, v = self.ex.prefill(prefix_dev, prefix_mask, params, keys=st["keys"], values=st["values"])
-        keys, values = DeviceArray(k), DeviceArray(v)
-        num_valid = nvs[0] if b == 1 else nvs
-        return keys, values, prefix_mask, suffix_cos, suffix_sin, num_valid
+        out = (to_device(np.concatenate(masks, 0), "float32", dev),
+               to_device(np.concatenate(coss, 0), "float32", dev),
+               to_device(np.concatenate(sins, 0), "float32", dev), nvs)
+        if len(self._tables) > 256:
+            self._tables.clear()
+        self._tables[key] = out
+        return out
+
+    def _time_table(self, n: int) -> torch.Tensor:
+        """make_time_embs(n, W1) stacked [n, W1] in the model dtype, on the device (cached)."""
+        key = ("time", n)
+        if key not in self._tables:
+            te = np.concatenate(make_time_embs(n, self.config.action_expert.width), axis=0)
+            self._tables[key] = to_device(te, self._dt(), self.dev)
+        return self._tables[key]
 
     def _noise(self, noise, seed, batch=1):
         cfg = self.config
@@ -182,8 +209,7 @@ class PiZeroRunner:
         st["pmask"].copy_(pmask.torch if isinstance(pmask, DeviceArray) else pmask)
         st["scos"].copy_(scos)
         st["ssin"].copy_(ssin)
-        te = np.concatenate(make_time_embs(n, cfg.action_expert.width), axis=0)
-        st["te"].copy_(to_device(te, self._dt(), self.dev))
+        st["te"].copy_(self._time_table(n))
         self.ex.denoise_loop_kv(keys.torch, values.torch, st["x0"], st["te"], st["scos"],
                                 st["ssin"], st["pmask"], params, out=st["x"])
         return st["x"].cpu().numpy()
