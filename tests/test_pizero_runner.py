@@ -92,3 +92,28 @@ def test_vm_function_contract(runner, loaded):
     tes = np.concatenate(make_time_embs(cfg.num_denoise_steps, cfg.action_expert.width), 0)
     out = vm["denoise_loop_kv"](keys, values, x0, tes.astype(np.float16), c, s, pm, params).numpy()
     assert out.shape == (1, cfg.action_horizon, cfg.action_dim) and np.all(np.isfinite(out))
+
+
+def test_cached_tables_follow_the_pad_pattern(runner, loaded):
+    """The runner keeps the pad mask, suffix RoPE tables and time embeddings on the device, keyed
+    by the pad pattern: alternating patterns give each pattern's own result, identical to a
+    fresh runner's (the tables are recomputed there)."""
+    from mlc_vla.model.pi0 import Pi0Config
+    from mlc_vla.sample import PiZeroRunner
+
+    params, prefix = loaded
+    cfg = runner.config
+    noise = np.random.default_rng(5).standard_normal(
+        (1, cfg.action_horizon, cfg.action_dim)).astype("float32")
+    pad_a = np.ones((cfg.prefix_len,), np.float32)
+    pad_a[-100:] = 0.0
+    pad_b = np.ones((cfg.prefix_len,), np.float32)
+    pad_b[300:400] = 0.0
+    outs = [runner.sample_graph(params, prefix, noise=noise, prefix_pad=p)
+            for p in (pad_a, pad_b, None, pad_a)]
+    assert np.array_equal(outs[0], outs[3])
+    assert not np.array_equal(outs[0], outs[1]) and not np.array_equal(outs[0], outs[2])
+    fresh = PiZeroRunner(Pi0Config(**DUMMY_KWARGS), target="cuda")
+    fparams = fresh.to_params(list(params))
+    assert np.array_equal(fresh.sample_graph(fparams, prefix, noise=noise, prefix_pad=pad_b),
+                          outs[1])
