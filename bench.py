@@ -329,9 +329,15 @@ def run_b200(args):
 
     cfg = full_config()
     B = args.batch
-    runner = PiZeroRunner(cfg, target="cuda", max_batch=B, device=local)
+    quant = None
+    if args.quant != "none":
+        from mlc_vla.quant import PRESETS
+
+        quant = PRESETS[args.quant]
+    runner = PiZeroRunner(cfg, target="cuda", max_batch=B, device=local, quant=quant)
     rt = runner.ex
-    params = make_weights(rt.named_params, dev, seed=0)
+    params = (make_weights(rt.named_params, dev, seed=0) if quant is None
+              else rt.to_params(make_quant_weights(cfg, quant, dev, seed=0)))
     rt.bind(params)
     lib = _lib.load()
 
@@ -457,9 +463,11 @@ def run_b200(args):
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
             "data": "synthetic (random N(0,0.02) weights, N(0,1) prefix_embs and noise, seeded)",
             "config": {"workload": "pi0.5 fp16, per GPU batch %d: prefill(968) + denoise_loop_kv "
-                                   "(10 Euler steps, one CUDA graph); horizon 50, action_dim 32%s"
+                                   "(10 Euler steps, one CUDA graph); horizon 50, action_dim 32%s%s"
                                    % (B, "; valid prefix lengths U[700,968], padded with the mask"
-                                      if args.pad else ""),
+                                      if args.pad else "",
+                                      "" if quant is None else f"; weights {args.quant} (the denoise "
+                                      "GEMMs read the codes, prefill reads them dequantised)"),
                        "model": "pi0.5 (gemma_2b prefix expert + gemma_300m action expert)",
                        "global_batch": world * B, "seq_len": P, "parallelism": f"dp{world} (replicas)",
                        "l2": "inputs larger than L2 (4.8 GB of weights streamed per chunk)"},
@@ -559,7 +567,7 @@ def main():
     ap.add_argument("--part", default="chunk", choices=["chunk", "prefill", "step"],
                     help="profiling aid: time only the prefill or one denoise step")
     ap.add_argument("--quant", default="none", choices=["none", "q4f16_1", "q3f16_1"],
-                    help="with --part: group-quantised weights (fused dequant in the denoise GEMMs)")
+                    help="group-quantised weights (the denoise GEMMs dequantise in shared memory)")
     ap.add_argument("--layers", type=int, default=18, choices=[2, 18],
                     help="with --part: 2 = full widths with two layers, for small profiler captures")
     args = ap.parse_args()

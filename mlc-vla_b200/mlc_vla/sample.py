@@ -79,13 +79,14 @@ class PiZeroRunner:
     """Builds the M1 runtime on a B200 and drives the denoising loop from the host."""
 
     def __init__(self, config: Pi0Config, target: str = "cuda", cuda_graph: bool = False,
-                 cublas=None, max_batch: int = 1, device: Optional[int] = None):
+                 cublas=None, max_batch: int = 1, device: Optional[int] = None, quant=None):
         self.config = config
         self.target = target
         self.cuda_graph = cuda_graph
         self.ex, self.named_params = compile_model(config, target, functions=_KV_FUNCS,
                                                    cuda_graph=cuda_graph, cublas=cublas,
-                                                   max_batch=max_batch, device=device)
+                                                   max_batch=max_batch, device=device,
+                                                   quant=quant)
         # this build issues no cuBLAS call: every GEMM is one of its own kernels
         self.cublas = False
         self.dev = self.ex.device
