@@ -119,6 +119,16 @@ int pi0_quantize_weight(int quant, int dtype, const void* w, int64_t n_out, int6
 int pi0_dequantize_weight(int quant, int dtype, const uint32_t* q_weight, const void* q_scale,
                           int64_t n_out, int64_t k, void* w, pi0_stream_t stream);
 
+/* vm["embed_language"] (python/mlc_vla/model/pi0/pi0_model.py:101-104, spec :217-220; the prefix
+ * expert's token embedding before prefix assembly): out[t, :] = table[input_ids[t], :] · sqrt(width)
+ * in the model dtype (the constant rounded to that dtype, one rounding of the product).
+ * table [vocab, width] (embed_tokens.weight, PaliGemma vocab 257152), input_ids [n_tokens] int32,
+ * out [n_tokens, width]; width a multiple of 8. An id outside [0, vocab) yields a zero row and
+ * sets the device int *err to 1 (err may be NULL). Context-free. */
+int pi0_embed_language(int dtype, const void* table, int64_t vocab, int width,
+                       const int32_t* input_ids, int n_tokens, void* out, int* err,
+                       pi0_stream_t stream);
+
 /* ---- building block and measurement hooks (no counterpart in the reference) --------------- */
 
 /* y[M, N] = x[M, K] · w[N, K]^T in the context's model dtype (fp32 accumulation, one rounding):

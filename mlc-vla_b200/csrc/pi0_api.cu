@@ -1644,6 +1644,28 @@ int pi0_div_check(const float* a, const float* b, float* out, int64_t n, pi0_str
   return cudaGetLastError() == cudaSuccess ? 0 : PI0_ERR_CUDA;
 }
 
+int pi0_embed_language(int dtype, const void* table, int64_t vocab, int width,
+                       const int32_t* input_ids, int n_tokens, void* out, int* err,
+                       pi0_stream_t stream) {
+  if (!table || !input_ids || !out || vocab < 1 || width < 8 || width % 8 || n_tokens < 0)
+    return PI0_ERR_INVALID;
+  if (n_tokens == 0) return 0;
+  const int threads = std::min(256, std::max(32, width / 8));
+  const double c = std::sqrt((double)width);
+  if (dtype == PI0_F16) {
+    embed_language_kernel<__half><<<n_tokens, threads, 0, stream>>>(
+        (const __half*)table, vocab, width, input_ids, (__half*)out,
+        __half2float(__float2half_rn((float)c)), err);
+  } else if (dtype == PI0_BF16) {
+    embed_language_kernel<__nv_bfloat16><<<n_tokens, threads, 0, stream>>>(
+        (const __nv_bfloat16*)table, vocab, width, input_ids, (__nv_bfloat16*)out,
+        __bfloat162float(__float2bfloat16_rn((float)c)), err);
+  } else {
+    return PI0_ERR_INVALID;
+  }
+  return cudaGetLastError() == cudaSuccess ? 0 : PI0_ERR_CUDA;
+}
+
 int pi0_device_error(pi0_ctx* ctx) {
   if (!ctx) return PI0_ERR_INVALID;
   CK(cudaSetDevice(ctx->device));

@@ -251,6 +251,30 @@ __global__ void dequantize_kernel(const uint32_t* __restrict__ qw, const T* __re
   w[id] = Tr<T>::t(((float)code - (float)maxint) * s);
 }
 
+// Language embedding (pi0_model.py:101-104, embed_language): out[t, :] = RN(table[id_t, :] · c)
+// with c = sqrt(width) rounded to the model dtype (the Python constant takes the tensor's dtype),
+// the product exact in fp32 and rounded once. One block per token, 16-byte chunks; an id outside
+// [0, vocab) gives a zero row and sets *err to 1 (err may be null).
+template <typename T>
+__global__ void embed_language_kernel(const T* __restrict__ table, int64_t vocab, int width,
+                                      const int* __restrict__ ids, T* __restrict__ out, float c,
+                                      int* err) {
+  const int t = blockIdx.x;
+  const int id = ids[t];
+  const bool in = id >= 0 && (int64_t)id < vocab;
+  if (!in && threadIdx.x == 0 && err) atomicExch(err, 1);
+  const uint4* src = reinterpret_cast<const uint4*>(table + (in ? (size_t)id : 0) * width);
+  uint4* dst = reinterpret_cast<uint4*>(out + (size_t)t * width);
+  for (int i = threadIdx.x; i < width / 8; i += blockDim.x) {
+    uint4 v = in ? src[i] : make_uint4(0, 0, 0, 0);
+    const T* e = reinterpret_cast<const T*>(&v);
+    uint32_t o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) o[j] = Tr<T>::pack(Tr<T>::f(e[2 * j]) * c, Tr<T>::f(e[2 * j + 1]) * c);
+    dst[i] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
 // a / b through div_by_rcp (common.cuh), for the bit-for-bit comparison with IEEE division
 __global__ void div_check_kernel(const float* __restrict__ a, const float* __restrict__ b,
                                  float* __restrict__ out, int64_t n) {

@@ -362,5 +362,29 @@ def dequantize_weight(q_weight: torch.Tensor, q_scale: torch.Tensor, preset, k: 
     return w
 
 
+def embed_language(table: torch.Tensor, input_ids, err: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``vm["embed_language"]`` (``pi0_model.py:101-104``): token ids [.., T] -> embeddings
+    [.., T, width] = table[id] · sqrt(width) in the table's dtype (fp16 / bf16), on the table's
+    device. Raises ValueError for an id outside the table unless `err` (a device int32 tensor)
+    is given, in which case it is set to 1 and the row is zero."""
+    lib = _lib.load()
+    if table.dim() != 2 or not table.is_cuda:
+        raise ValueError("table must be a [vocab, width] CUDA tensor")
+    dev = table.device
+    ids = torch.as_tensor(np.asarray(input_ids) if not isinstance(input_ids, torch.Tensor)
+                          else input_ids).to(device=dev, dtype=torch.int32).contiguous()
+    out = torch.empty(tuple(ids.shape) + (table.shape[1],), dtype=table.dtype, device=dev)
+    own = err is None
+    flag = torch.zeros(1, dtype=torch.int32, device=dev) if own else err
+    dcode = _lib.DTYPE_CODE[str(table.dtype).replace("torch.", "")]
+    s = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+    _lib.check(lib.pi0_embed_language(dcode, table.contiguous().data_ptr(), table.shape[0],
+                                      table.shape[1], ids.data_ptr(), ids.numel(), out.data_ptr(),
+                                      flag.data_ptr(), s), None, "pi0_embed_language")
+    if own and int(flag.item()):
+        raise ValueError("input_ids holds an id outside the embedding table")
+    return out
+
+
 __all__ = ["Pi0Runtime", "DeviceArray", "ParamSpec", "to_device", "quantize_weight",
-           "dequantize_weight"]
+           "dequantize_weight", "embed_language"]

@@ -22,6 +22,7 @@ Followed code (paths relative to the reference project):
 * ``python/mlc_vla/model/pi0/pi0_model.py:29-41``    joint additive mask
 * ``pi0_model.py:106-194``                           _time_cond, denoise_step (M0), prefill,
                                                      denoise_step_kv, denoise_loop_kv
+* ``pi0_model.py:101-104``                           embed_language (gather · sqrt(width))
 
 Rounding conventions (the reference's TVM lowering is not available to pin them to the
 ulp): a model-dtype matmul accumulates in fp32 and rounds once; a Linear with bias rounds
@@ -470,3 +471,17 @@ def random_params(named_params: Sequence, seed: int = 0, scale: float = 0.02) ->
         else:
             out[name] = (scale * rng.standard_normal(shape)).astype(F32)
     return out
+
+
+def embed_language(table, input_ids, dtype: str) -> np.ndarray:
+    """pi0_model.py:101-104: ``embed_tokens(input_ids) * math.sqrt(width)`` with the table in the
+    model dtype. The Python constant takes the tensor's dtype, so it is rounded to that dtype
+    first; the product (exact in fp32) is rounded once. Ids outside the table give zero rows."""
+    table = np.asarray(table)
+    ids = np.asarray(input_ids).reshape(-1).astype(np.int64)
+    width = table.shape[1]
+    c = rnd(np.float32(math.sqrt(width)), dtype).astype(np.float32)
+    ok = (ids >= 0) & (ids < table.shape[0])
+    rows = rnd(table, dtype).astype(np.float32)[np.where(ok, ids, 0)]
+    rows[~ok] = 0.0
+    return rnd(rows * c, dtype)

@@ -154,3 +154,18 @@ def test_oracle_pad_invariance():
     a = run(full, prefix)
     b = run(trunc, prefix[:, :V].copy())
     assert cosine(a, b) >= 0.9999
+
+
+def test_embed_language_oracle_formula():
+    """embed_language = table[id] · sqrt(width), the constant in the model dtype
+    (pi0_model.py:101-104): sqrt(2048) is 45.25 in fp16 and bf16."""
+    from oracle import pi0_oracle as O
+
+    table = np.arange(4 * 2048, dtype=np.float32).reshape(4, 2048) / 4096.0
+    out = O.embed_language(table, np.array([[2, 0]]), "float16")
+    c = np.float32(np.float16(np.sqrt(2048.0)))
+    assert c == np.float32(45.25)
+    want = (np.float16(table[[2, 0]]).astype(np.float32) * c).astype(np.float16)
+    assert np.array_equal(out.reshape(2, 2048), want)
+    out32 = O.embed_language(table, np.array([1]), "float32")
+    assert np.allclose(out32, table[1] * np.float32(np.sqrt(2048.0)))
