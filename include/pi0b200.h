@@ -100,6 +100,15 @@ int pi0_denoise_step_kv(pi0_ctx* ctx, int batch, const float* keys, const void* 
                         const float* suffix_sin, const float* prefix_mask, float* v_out,
                         pi0_stream_t stream);
 
+/* vm["denoise_step"], the M0 joint step (pi0_model.py:111-125; gemma_dual.py:162-233): one
+ * denoising step of both experts over [prefix; suffix] with the joint mask (all prefix tokens
+ * valid; suffix RoPE positions P .. P+S-1). Computed as the prefix expert's pass into a K/V cache
+ * the context owns, then the suffix step on it: the joint mask lets no prefix token see the
+ * suffix, so this is the same function (the M1 ≡ M0 identity). prefix_embs [B, P, W0], x_t
+ * [B, S, D] model dtype, time_emb [1, W1]; v_out [B, S, D] fp32. */
+int pi0_denoise_step(pi0_ctx* ctx, int batch, const void* prefix_embs, const void* x_t,
+                     const void* time_emb, float* v_out, pi0_stream_t stream);
+
 /* vm["denoise_loop_kv"] (pi0_model.py:165-194): cfg.num_denoise_steps Euler steps
  * (dt = -1/N, x in fp32), replayed as one CUDA graph per distinct argument set. x_out may
  * alias x0. */

@@ -106,6 +106,10 @@ struct pi0_ctx {
   int* perm_gu1 = nullptr; // ... for F1
   float* rope_cos = nullptr;  // prefix RoPE table [P, hd/2]
   float* rope_sin = nullptr;
+  // the M0 joint denoise_step: its own prefix K/V cache, an all-valid prefix mask and the suffix
+  // RoPE tables at positions P .. P+S-1, for every request of a batch
+  float *m0_keys = nullptr, *m0_mask = nullptr, *m0_cos = nullptr, *m0_sin = nullptr;
+  void* m0_values = nullptr;
 
   // workspaces
   void *xp = nullptr, *xpn = nullptr, *attn_p = nullptr, *hp = nullptr;
@@ -1148,6 +1152,25 @@ int alloc_all(pi0_ctx* ctx) {
     TRY(dev_alloc(ctx, &ctx->kpre16, (size_t)g.depth * B * hkv * P * e));
     TRY(dev_alloc(ctx, &ctx->ksuf16, B * hkv * S * e));
   }
+  {
+    const size_t kvn = (size_t)g.depth * B * KV * P * hd;
+    TRY(dev_alloc(ctx, (void**)&ctx->m0_keys, kvn * 4));
+    TRY(dev_alloc(ctx, &ctx->m0_values, kvn * e));
+    TRY(dev_alloc(ctx, (void**)&ctx->m0_mask, B * P * 4));
+    CK(cudaMemset(ctx->m0_mask, 0, B * P * 4));
+    std::vector<float> c(B * S * (hd / 2)), sn(B * S * (hd / 2));
+    for (size_t bb = 0; bb < B; ++bb)
+      for (size_t t = 0; t < S; ++t)
+        for (int i = 0; i < hd / 2; ++i) {  // float64 -> fp32, as the prefix table above
+          const double r = (double)(P + t) / std::pow((double)g.rope_theta, (2.0 / hd) * i);
+          c[(bb * S + t) * (hd / 2) + i] = (float)std::cos(r);
+          sn[(bb * S + t) * (hd / 2) + i] = (float)std::sin(r);
+        }
+    TRY(dev_alloc(ctx, (void**)&ctx->m0_cos, c.size() * 4));
+    TRY(dev_alloc(ctx, (void**)&ctx->m0_sin, sn.size() * 4));
+    CK(cudaMemcpy(ctx->m0_cos, c.data(), c.size() * 4, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(ctx->m0_sin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice));
+  }
   TRY(dev_alloc(ctx, &ctx->t1, (size_t)N * W1 * e));
   TRY(dev_alloc(ctx, &ctx->cond, (size_t)N * W1 * e));
   TRY(dev_alloc(ctx, &ctx->mods, (size_t)N * nmodw * e));
@@ -1472,6 +1495,29 @@ int pi0_denoise_step_kv(pi0_ctx* ctx, int batch, const float* keys, const void* 
     return run_step<__half>(ctx, batch, keys, (const __half*)values, (const __half*)x_t,
                             (const __half*)time_emb, suffix_cos, suffix_sin, prefix_mask, v_out,
                             st);
+  };
+  if (ctx->prof_on) return run_profiled(ctx, stream, body);
+  return body(stream);
+}
+
+int pi0_denoise_step(pi0_ctx* ctx, int batch, const void* prefix_embs, const void* x_t,
+                     const void* time_emb, float* v_out, pi0_stream_t stream) {
+  TRY(check_ready(ctx, batch));
+  if (!prefix_embs || !x_t || !time_emb || !v_out)
+    return fail(ctx, PI0_ERR_INVALID, "null tensor argument");
+  auto body = [&](cudaStream_t st) {
+    if (is_bf16(ctx)) {
+      using T = __nv_bfloat16;
+      TRY(run_prefill<T>(ctx, batch, (const T*)prefix_embs, ctx->m0_mask, ctx->m0_keys,
+                         (T*)ctx->m0_values, st));
+      return run_step<T>(ctx, batch, ctx->m0_keys, (const T*)ctx->m0_values, (const T*)x_t,
+                         (const T*)time_emb, ctx->m0_cos, ctx->m0_sin, ctx->m0_mask, v_out, st);
+    }
+    using T = __half;
+    TRY(run_prefill<T>(ctx, batch, (const T*)prefix_embs, ctx->m0_mask, ctx->m0_keys,
+                       (T*)ctx->m0_values, st));
+    return run_step<T>(ctx, batch, ctx->m0_keys, (const T*)ctx->m0_values, (const T*)x_t,
+                       (const T*)time_emb, ctx->m0_cos, ctx->m0_sin, ctx->m0_mask, v_out, st);
   };
   if (ctx->prof_on) return run_profiled(ctx, stream, body);
   return body(stream);

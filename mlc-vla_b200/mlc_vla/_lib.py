@@ -37,7 +37,7 @@ EXPORTED = (
     "pi0_quantize_weight", "pi0_dequantize_weight", "pi0_launch_count", "pi0_profile_enable",
     "pi0_profile_read", "pi0_profile_families", "pi0_profile_family_name", "pi0_linear",
     "pi0_device_error", "pi0_div_check", "pi0_linear_noalloc", "pi0_wait_check",
-    "pi0_embed_language",
+    "pi0_embed_language", "pi0_denoise_step",
 )
 
 
@@ -125,6 +125,7 @@ def load():
         lib.pi0_device_error.argtypes = [vp]
         lib.pi0_div_check.argtypes = [vp, vp, vp, i64, vp]
         lib.pi0_embed_language.argtypes = [i32, vp, i64, i32, vp, i32, vp, vp, vp]
+        lib.pi0_denoise_step.argtypes = [vp, i32, vp, vp, vp, vp, vp]
         lib.pi0_wait_check.argtypes = [vp, i32, vp]
         lib.pi0_linear_noalloc.argtypes = [i32, vp, i32, i32, vp, i32, vp, vp]
         for name in EXPORTED:

@@ -30,7 +30,7 @@ from typing import Dict, List, Optional, Sequence, Tuple
 
 from .pi0_config import Pi0Config
 
-FUNCTIONS = ("prefill", "denoise_step_kv", "denoise_loop_kv")
+FUNCTIONS = ("prefill", "denoise_step_kv", "denoise_loop_kv", "denoise_step")
 
 
 @dataclasses.dataclass(frozen=True)
@@ -143,7 +143,7 @@ def backbone_named_params(config: Pi0Config, dtype: Optional[str] = None,
 
 
 def function_specs(config: Pi0Config, batch: int = 1) -> Dict[str, List[Tuple[str, Tuple[int, ...], str]]]:
-    """Argument names, shapes and dtypes of the three exported functions.
+    """Argument names, shapes and dtypes of the exported functions.
 
     Mirrors ``Pi0Model.get_default_spec`` (``pi0_model.py:197-255``): the reference fixes the
     batch at 1; ``batch`` here extends every per-request tensor with a leading ``B`` (keys and
@@ -162,6 +162,8 @@ def function_specs(config: Pi0Config, batch: int = 1) -> Dict[str, List[Tuple[st
                             ("x_t", act, dt), ("time_emb", (1, ae.width), dt),
                             ("suffix_cos", rope, "float32"), ("suffix_sin", rope, "float32"),
                             ("prefix_mask", mask, "float32")],
+        "denoise_step": [("prefix_embs", (batch, config.prefix_len, vlm.width), dt),
+                         ("x_t", act, dt), ("time_emb", (1, ae.width), dt)],
         "denoise_loop_kv": [("keys", kv_shape, "float32"), ("values", kv_shape, dt),
                             ("x0", act, "float32"),
                             ("time_embs", (config.num_denoise_steps, ae.width), dt),

@@ -273,6 +273,27 @@ class Pi0Runtime:
         self._hold = (k, v, x, te, sc, ss, m)
         return out
 
+    def denoise_step(self, prefix_embs, x_t, time_emb, params=None, out=None):
+        """M0 joint step (``pi0_model.py:111-125``): prefix expert over the whole (all-valid)
+        prefix and action expert over the suffix, v_t [B, S, D] fp32."""
+        if params is not None:
+            self.bind(params)
+        c = self.config
+        p = self._t(prefix_embs, self.dtype)
+        b = self._batch_of(p, c.prefix_len * c.vlm.width)
+        x = self._t(x_t, self.dtype)
+        te = self._t(time_emb, self.dtype)
+        if x.numel() != b * c.action_horizon * c.action_dim or te.numel() != c.action_expert.width:
+            raise ValueError("x_t must be [B, S, D] and time_emb [1, W1]")
+        if out is None:
+            out = torch.empty((b, c.action_horizon, c.action_dim), dtype=torch.float32,
+                              device=self.device)
+        _lib.check(self.lib.pi0_denoise_step(self._ctx, b, p.data_ptr(), x.data_ptr(),
+                                             te.data_ptr(), out.data_ptr(), self._stream()),
+                   self._ctx, "pi0_denoise_step")
+        self._hold = (p, x, te)
+        return out
+
     def denoise_loop_kv(self, keys, values, x0, time_embs, suffix_cos, suffix_sin, prefix_mask,
                         params=None, out=None):
         if params is not None:
@@ -325,9 +346,12 @@ class Pi0Runtime:
             def f(keys, values, x0, time_embs, suffix_cos, suffix_sin, prefix_mask, params):
                 return DeviceArray(self.denoise_loop_kv(keys, values, x0, time_embs, suffix_cos,
                                                         suffix_sin, prefix_mask, params))
+        elif name == "denoise_step":
+            def f(prefix_embs, x_t, time_emb, params):
+                return DeviceArray(self.denoise_step(prefix_embs, x_t, time_emb, params))
         else:
-            raise KeyError(f"{name!r} is not an exported function of the M1 path "
-                           f"(prefill, denoise_step_kv, denoise_loop_kv)")
+            raise KeyError(f"{name!r} is not an exported function of this build "
+                           f"(prefill, denoise_step_kv, denoise_loop_kv, denoise_step)")
         return f
 
 

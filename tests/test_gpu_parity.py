@@ -240,3 +240,41 @@ def test_batch_beyond_weight_streaming_rows():
         xo = O.denoise_loop_kv(m.p, cfg, ko, vo, inp["noise"][i:i + 1], te, sc[i:i + 1],
                                ss[i:i + 1], pm[i:i + 1])
         _check(xb[i:i + 1], xo, what=f"batch-20 request {i} (valid {nvs[i]})")
+
+
+def test_m0_denoise_step_matches_oracle_and_m1(mini):
+    """vm["denoise_step"] (M0 joint step, pi0_model.py:111-125) on the GPU: against the oracle's
+    M0 step (gemma_dual.py:162-233 restated) and bit-identical to prefill + denoise_step_kv with
+    an all-valid prefix (the M1 ≡ M0 identity, compare_kv.py:39-116)."""
+    cfg = mini.cfg
+    inp = mini.inputs(seed=4)
+    v0 = _np(mini.rt.denoise_step(inp["prefix"], inp["x_t"], inp["time_emb"]))
+    assert mini.rt.device_error() == 0
+    vo = O.denoise_step(mini.p, cfg, inp["prefix"], inp["x_t"], inp["time_emb"])
+    _check(v0, vo, what="M0 denoise_step vs oracle M0")
+    pm = O.prefix_mask(cfg.prefix_len)
+    sc, ss = O.suffix_rope(cfg, cfg.prefix_len)
+    k, v = mini.rt.prefill(inp["prefix"], pm)
+    v1 = _np(mini.rt.denoise_step_kv(k, v, inp["x_t"], inp["time_emb"], sc, ss, pm))
+    assert np.array_equal(v0, v1)
+    # VM-style call, as the reference's compare_kv.py makes it
+    v2 = mini.rt["denoise_step"](inp["prefix"], inp["x_t"], inp["time_emb"], mini.params)
+    assert np.array_equal(v2.numpy(), v0)
+
+
+def test_m0_equals_m1_full_width():
+    """The M1 ≡ M0 gate at every π0.5 width (two layers): both computed on the GPU, bit-identical,
+    and the M0 step within the fp16 tolerance of the oracle."""
+    cfg = config(recipes.FULL2)
+    m = Model(cfg)
+    inp = m.inputs(seed=6)
+    v0 = _np(m.rt.denoise_step(inp["prefix"], inp["x_t"], inp["time_emb"]))
+    pm = O.prefix_mask(cfg.prefix_len)
+    sc, ss = O.suffix_rope(cfg, cfg.prefix_len)
+    k, v = m.rt.prefill(inp["prefix"], pm)
+    v1 = _np(m.rt.denoise_step_kv(k, v, inp["x_t"], inp["time_emb"], sc, ss, pm))
+    assert m.rt.device_error() == 0
+    assert np.array_equal(v0, v1)
+    ko, vo = m.oracle_kv(inp["prefix"], pm)
+    vref = O.denoise_step_kv(m.p, cfg, ko, vo, inp["x_t"], inp["time_emb"], sc, ss, pm)
+    _check(v0, vref, what="M0 full width vs oracle")
