@@ -41,3 +41,16 @@ def test_compare_quant(quant):
     cfg = Pi0Config(paligemma_variant="dummy", action_expert_variant="dummy", max_token_len=16,
                     action_horizon=4)
     assert compare_quant.run(cfg, "cuda", quant, seed=0)
+
+
+@pytest.mark.parametrize("quant", [None, "q4f16_1"])
+def test_bench_kv_dummy(quant):
+    from mlc_vla import bench_kv
+    from mlc_vla.model.pi0 import Pi0Config
+
+    cfg = Pi0Config(paligemma_variant="dummy", action_expert_variant="dummy", max_token_len=16,
+                    action_horizon=4)
+    out = bench_kv.run(cfg, "cuda", steps=3, iters=3, quant=quant)
+    assert out["prefill_ms"] > 0 and out["step_kv_ms"] > 0
+    if quant is None:
+        assert out["step_m0_ms"] > 0
