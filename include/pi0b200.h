@@ -132,7 +132,8 @@ int pi0_dequantize_weight(int quant, int dtype, const uint32_t* q_weight, const 
  * expert's token embedding before prefix assembly): out[t, :] = table[input_ids[t], :] · sqrt(width)
  * in the model dtype (the constant rounded to that dtype, one rounding of the product).
  * table [vocab, width] (embed_tokens.weight, PaliGemma vocab 257152), input_ids [n_tokens] int32,
- * out [n_tokens, width]; width a multiple of 8. An id outside [0, vocab) yields a zero row and
+ * out [n_tokens, width]; width a multiple of 8, table and out 16-byte aligned (PI0_ERR_INVALID
+ * otherwise). An id outside [0, vocab) yields a zero row and
  * sets the device int *err to 1 (err may be NULL). Context-free. */
 int pi0_embed_language(int dtype, const void* table, int64_t vocab, int width,
                        const int32_t* input_ids, int n_tokens, void* out, int* err,

@@ -1695,6 +1695,9 @@ int pi0_embed_language(int dtype, const void* table, int64_t vocab, int width,
                        pi0_stream_t stream) {
   if (!table || !input_ids || !out || vocab < 1 || width < 8 || width % 8 || n_tokens < 0)
     return PI0_ERR_INVALID;
+  // rows are moved in 16-byte vectors
+  if ((reinterpret_cast<uintptr_t>(table) | reinterpret_cast<uintptr_t>(out)) & 15)
+    return PI0_ERR_INVALID;
   if (n_tokens == 0) return 0;
   const int threads = std::min(256, std::max(32, width / 8));
   const double c = std::sqrt((double)width);

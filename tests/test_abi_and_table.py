@@ -128,3 +128,20 @@ def test_cpu_targets_are_refused():
 
     with pytest.raises(ValueError, match="CUDA"):
         compile_model(Pi0Config(**{**recipes.MINI, "dtype": "float16"}), "c")
+
+
+def test_embed_language_rejects_bad_arguments_before_any_device_work():
+    """pi0_embed_language checks its arguments on the host (no GPU needed): null pointers,
+    a width that is not a multiple of 8, and table / out pointers off a 16-byte boundary."""
+    import ctypes
+
+    from mlc_vla import _lib
+
+    lib = _lib.load()
+    vp = ctypes.c_void_p
+    ok_ptr, bad_ptr = vp(0x100000), vp(0x100008)
+    assert lib.pi0_embed_language(_lib.PI0_F16, None, 10, 64, ok_ptr, 1, ok_ptr, None, None) == 1
+    assert lib.pi0_embed_language(_lib.PI0_F16, ok_ptr, 10, 60, ok_ptr, 1, ok_ptr, None, None) == 1
+    assert lib.pi0_embed_language(_lib.PI0_F16, bad_ptr, 10, 64, ok_ptr, 1, ok_ptr, None, None) == 1
+    assert lib.pi0_embed_language(_lib.PI0_F16, ok_ptr, 10, 64, ok_ptr, 1, bad_ptr, None, None) == 1
+    assert lib.pi0_embed_language(_lib.PI0_F16, ok_ptr, 10, 64, ok_ptr, 0, ok_ptr, None, None) == 0
