@@ -13,12 +13,12 @@ actions down) over the same steps.
 
 Prints one JSON line on rank 0 (schema in the project's build notes): value = chunks/s over all
 GPUs, ms_per_step = ms per chunk (per GPU), roofline of the dominant kernel family measured
-live with CUDA events, the CPU oracle timed on a bounded sample as ``cpu_baseline``, SM clocks
+live with CUDA events, the CPU oracle timed on one whole chunk as ``cpu_baseline``, SM clocks
 sampled during the timed region, and the number of library kernels launched.
 
 ``--impl reference`` times the reference's CPU implementation of the path — the numpy oracle
-that restates it (the reference itself needs TVM, absent here) — on the host cores, on a
-bounded sample per step, and prints the same line with ``"impl": "reference"``.
+that restates it (the reference itself needs TVM, absent here) — on all host cores, one whole
+chunk per step, and prints the same line with ``"impl": "reference"``.
 """
 
 from __future__ import annotations
@@ -29,6 +29,7 @@ import json
 import os
 import subprocess
 import sys
+import tempfile
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
@@ -51,10 +52,13 @@ def peaks():
     return dict(FALLBACK_PEAKS), "fallback"
 
 
-def full_config():
+def full_config(logits="float32"):
+    """The benchmarked π0.5 configuration; ``logits`` is the reference's attn_logits_dtype
+    (its default "float32", or "float16" for its tensor-core option)."""
     from mlc_vla.model.pi0 import Pi0Config
 
-    return Pi0Config(action_horizon=50, action_dim=32, num_denoise_steps=10, dtype="float16")
+    return Pi0Config(action_horizon=50, action_dim=32, num_denoise_steps=10, dtype="float16",
+                     attn_logits_dtype=logits)
 
 
 # ------------------------------------------------------------------------------------------
@@ -119,11 +123,12 @@ class ClockSampler:
     def __init__(self, gpu_index):
         self.gpu = gpu_index
         self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_gpu{gpu_index}.csv")
+        # samples go to a private temporary file (removed after the summary is read)
+        fd, self.path = tempfile.mkstemp(prefix=f"pi0_clocks_gpu{gpu_index}_", suffix=".csv")
+        os.close(fd)
 
     def __enter__(self):
         try:
-            os.makedirs(os.path.dirname(self.path), exist_ok=True)
             self.f = open(self.path, "w")
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
@@ -158,6 +163,10 @@ class ClockSampler:
             for n, v in zip(names, f[5:9]):
                 if v.lower().startswith("active"):
                     reasons.add(n)
+        try:
+            os.unlink(self.path)
+        except OSError:
+            pass
         if not sm:
             return None
         return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons),
@@ -165,57 +174,74 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------------------------------
-# CPU baseline: the oracle on a bounded sample
+# CPU baseline: the oracle on whole chunks
 # ------------------------------------------------------------------------------------------
-def cpu_sample_chunk_ms(reps=1):
-    """Time the numpy oracle on a 2-layer model with every π0.5 width (prefill of 968 tokens and
-    one denoise step of 50 tokens) and scale to the 18-layer chunk:
-    prefill_18 ≈ 17 · t_prefill(2 layers: one full layer + the last layer's k/v), and
-    step_18 ≈ 9 · t_step(2 layers); chunk = prefill_18 + 10 · step_18."""
-    import torch
-
-    from mlc_vla.model.pi0 import Pi0Config
-    from mlc_vla.model.pi0.pi0_model import backbone_named_params
-    from oracle import pi0_oracle as O
-
-    cfg = Pi0Config(paligemma_variant="gemma_2b_2l", action_expert_variant="gemma_300m_2l",
-                    action_horizon=50, action_dim=32, num_denoise_steps=10, dtype="float16")
-    g = torch.Generator().manual_seed(0)
-    raw = {n: (0.02 * torch.randn(s.shape, generator=g)).numpy() for n, s in backbone_named_params(cfg)}
-    p = O.prepare_params(raw, "float16")
-    rng = np.random.default_rng(1)
-    prefix = rng.standard_normal((1, cfg.prefix_len, cfg.vlm.width)).astype(np.float32)
-    x_t = rng.standard_normal((1, 50, 32)).astype(np.float32)
-    te = O.sinusoidal_time_emb(1.0, cfg.action_expert.width)
-    pm = O.prefix_mask(cfg.prefix_len)
-    sc, ss = O.suffix_rope(cfg, cfg.prefix_len)
-    tp, ts = [], []
-    for _ in range(reps):
-        t0 = time.perf_counter()
-        k, v = O.prefill(p, cfg, prefix, pm)
-        t1 = time.perf_counter()
-        O.denoise_step_kv(p, cfg, k, v, x_t, te, sc, ss, pm)
-        t2 = time.perf_counter()
-        tp.append(t1 - t0)
-        ts.append(t2 - t1)
-    tpre, tstep = float(np.median(tp)), float(np.median(ts))
-    chunk_ms = (17 * tpre + 10 * 9 * tstep) * 1e3
-    return chunk_ms, {"prefill_2layers_ms": tpre * 1e3, "step_2layers_ms": tstep * 1e3}
-
-
-def blas_threads():
+def cpu_threads():
+    """Use every host core for the oracle's BLAS calls, also under torchrun (which exports
+    OMP_NUM_THREADS=1), and return the count in use."""
+    n = os.cpu_count() or 1
     try:
-        from threadpoolctl import threadpool_info
+        from threadpoolctl import threadpool_info, threadpool_limits
 
-        n = [i.get("num_threads", 0) for i in threadpool_info() if i.get("user_api") == "blas"]
-        return max(n) if n else os.cpu_count()
+        threadpool_limits(n)
+        got = [i.get("num_threads", 0) for i in threadpool_info() if i.get("user_api") == "blas"]
+        return max(got) if got else n
     except Exception:  # noqa: BLE001
-        return os.cpu_count()
+        return n
 
 
-CPU_SAMPLE = ("numpy oracle (fp32 BLAS, fp16 rounding emulated) on a 2-layer model with every "
-              "pi0.5 width: prefill of 968 tokens + one 50-token denoise step, scaled to 18 layers "
-              "and 10 steps (17 x prefill + 90 x step)")
+class CpuChunk:
+    """The numpy oracle on the benchmarked workload: prefill of 968 tokens through all 18 prefix
+    layers plus the 10-step denoise loop through all 18 action-expert layers, fp16 rounding
+    emulated on fp32 BLAS. Every layer computes in full; to keep set-up short, all layers of an
+    expert share one seeded draw of that expert's layer weights (the arithmetic and the bytes
+    streamed per layer are those of distinct weights: a layer's 0.4 GB fp32 copy is far larger
+    than the host caches)."""
+
+    SAMPLE = ("numpy oracle (fp32 BLAS, fp16 rounding emulated): one whole chunk per step, "
+              "prefill(968) through 18 prefix layers + denoise_loop_kv (10 steps x 18 layers), "
+              "batch 1; layers of an expert share one weight draw")
+
+    def __init__(self):
+        from mlc_vla.model.pi0 import Pi0Config
+        from mlc_vla.model.pi0.pi0_model import backbone_named_params
+        from oracle import pi0_oracle as O
+
+        self.O = O
+        self.cores = cpu_threads()
+        cfg = Pi0Config(action_horizon=50, action_dim=32, num_denoise_steps=10, dtype="float16")
+        self.cfg = cfg
+        named = backbone_named_params(cfg)
+        rng = np.random.default_rng(0)
+        drawn, self.p = {}, {}
+        for name, spec in named:
+            # backbone.layers.<i>.<rest>: one draw per <rest>, shared by every layer i
+            parts = name.split(".")
+            key = ".".join(parts[3:]) if name.startswith("backbone.layers.") else name
+            if key not in drawn:
+                w = rng.standard_normal(tuple(int(x) for x in spec.shape), dtype=np.float32)
+                drawn[key] = O.rnd(w * np.float32(0.02), "float16")
+            self.p[name] = drawn[key]
+        P, S, D = cfg.prefix_len, cfg.suffix_len, cfg.action_dim
+        self.prefix = rng.standard_normal((1, P, cfg.vlm.width), dtype=np.float32)
+        self.noise = rng.standard_normal((1, S, D), dtype=np.float32)
+        self.pm = O.prefix_mask(P)
+        self.sc, self.ss = O.suffix_rope(cfg, P)
+        self.te = O.time_embs(cfg.num_denoise_steps, cfg.action_expert.width)
+
+    def chunk_ms(self):
+        O = self.O
+        t0 = time.perf_counter()
+        k, v = O.prefill(self.p, self.cfg, self.prefix, self.pm)
+        O.denoise_loop_kv(self.p, self.cfg, k, v, self.noise, self.te, self.sc, self.ss, self.pm)
+        return (time.perf_counter() - t0) * 1e3
+
+    def warm(self):
+        """A short untimed pass (one denoise step on a zero cache) that touches every code path."""
+        O, cfg = self.O, self.cfg
+        kv = (cfg.vlm.depth, 1, cfg.vlm.num_kv_heads, cfg.prefix_len, cfg.vlm.head_dim)
+        z = np.zeros(kv, np.float32)
+        O.denoise_step_kv(self.p, cfg, z, z, self.noise, self.te[:1], self.sc, self.ss, self.pm)
 
 
 # ------------------------------------------------------------------------------------------
@@ -225,13 +251,10 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
-    cores = blas_threads()
+    cpu = CpuChunk()
     for _ in range(args.warmup):
-        cpu_sample_chunk_ms()
-    t = []
-    for _ in range(args.steps):
-        ms, _ = cpu_sample_chunk_ms()
-        t.append(ms)
+        cpu.warm()
+    t = [cpu.chunk_ms() for _ in range(args.steps)]
     ms = float(np.mean(t))
     value = 1000.0 / ms
     line = {
@@ -241,8 +264,9 @@ def run_reference(args):
         "impl": "reference",
         "config": {"workload": "pi0.5 fp16 bs1: prefill(968) + 10 Euler steps (host CPU)",
                    "global_batch": 1, "seq_len": 968, "parallelism": "cpu"},
-        "cpu_baseline": {"value": value, "unit": "chunks/s", "cores": cores, "kind": "port",
-                         "sample": CPU_SAMPLE},
+        "cpu_baseline": {"value": value, "unit": "chunks/s", "cores": cpu.cores, "kind": "port",
+                         "sample": CpuChunk.SAMPLE + f"; {args.steps} chunks timed, warm-up: "
+                         f"{args.warmup} single denoise steps"},
         "e2e": {"value": value, "unit": "chunks/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -327,7 +351,7 @@ def run_b200(args):
         if world > 1:
             dist.barrier()
 
-    cfg = full_config()
+    cfg = full_config(args.attn_logits)
     B = args.batch
     quant = None
     if args.quant != "none":
@@ -452,9 +476,11 @@ def run_b200(args):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        cms, detail = cpu_sample_chunk_ms()
-        cpu = {"value": 1000.0 / cms, "unit": "chunks/s", "cores": blas_threads(), "kind": "port",
-               "sample": CPU_SAMPLE, **{k: round(v, 2) for k, v in detail.items()}}
+        c = CpuChunk()
+        c.warm()
+        cms = c.chunk_ms()
+        cpu = {"value": 1000.0 / cms, "unit": "chunks/s", "cores": c.cores, "kind": "port",
+               "sample": CpuChunk.SAMPLE + "; one chunk timed", "ms_per_chunk": round(cms, 1)}
 
     if rank == 0:
         line = {
@@ -470,6 +496,7 @@ def run_b200(args):
                                       "GEMMs read the codes, prefill reads them dequantised)"),
                        "model": "pi0.5 (gemma_2b prefix expert + gemma_300m action expert)",
                        "global_batch": world * B, "seq_len": P, "parallelism": f"dp{world} (replicas)",
+                       "attn_logits_dtype": args.attn_logits,
                        "l2": "inputs larger than L2 (4.8 GB of weights streamed per chunk)"},
             "e2e": e2e, "roofline": roofline, "cpu_baseline": cpu, "clocks": clk.summary(),
             "gpu_launches": int(n_launch),
@@ -493,7 +520,7 @@ def run_part(args):
 
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    cfg = full_config()
+    cfg = full_config(args.attn_logits)
     if args.layers == 2:  # profiling aid: every width of the full model, two layers
         cfg = dataclasses.replace(cfg, paligemma_variant="gemma_2b_2l",
                                   action_expert_variant="gemma_300m_2l")
@@ -568,6 +595,9 @@ def main():
                     help="profiling aid: time only the prefill or one denoise step")
     ap.add_argument("--quant", default="none", choices=["none", "q4f16_1", "q3f16_1"],
                     help="group-quantised weights (the denoise GEMMs dequantise in shared memory)")
+    ap.add_argument("--attn-logits", default="float32", choices=["float32", "float16"],
+                    help="attention logits operands (the reference's attn_logits_dtype; its "
+                         "default float32, or float16 for its tensor-core option)")
     ap.add_argument("--layers", type=int, default=18, choices=[2, 18],
                     help="with --part: 2 = full widths with two layers, for small profiler captures")
     args = ap.parse_args()

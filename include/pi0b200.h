@@ -56,6 +56,12 @@ enum pi0_dtype { PI0_F16 = 0, PI0_BF16 = 1, PI0_F32 = 2, PI0_U32 = 3 };
 enum pi0_quant { PI0_QUANT_NONE = 0, PI0_QUANT_Q4 = 1 /* q4f16_1 / q4bf16_1 */,
                  PI0_QUANT_Q3 = 2 /* q3f16_1 */ };
 
+/* Operand type of the attention logits q·kᵀ: the reference's Pi0Config.attn_logits_dtype
+ * (python/mlc_vla/model/pi0/pi0_config.py:97-102, gemma_dual.py:115), whose default is
+ * "float32" (fp32 q and k); the model dtype casts q and k to fp16 / bf16 first. Either way the
+ * product is accumulated in fp32. */
+enum pi0_logits { PI0_LOGITS_F32 = 0, PI0_LOGITS_MODEL_DTYPE = 1 };
+
 /* Model shape: the fields of Pi0Config / GemmaExpertConfig the backbone build reads
  * (python/mlc_vla/model/pi0/pi0_config.py:17-170). */
 typedef struct pi0_config {
@@ -69,6 +75,7 @@ typedef struct pi0_config {
   int32_t max_batch;                  /* workspace sizing; calls may use any B ≤ this */
   float rms_norm_eps;                 /* 1e-6 */
   float rope_theta;                   /* 1e4 */
+  int32_t attn_logits;                /* pi0_logits (zero: fp32, the reference's default) */
 } pi0_config;
 
 /* Replaces compile_model + relax.VirtualMachine (python/mlc_vla/sample.py:91-95,
@@ -153,15 +160,23 @@ int pi0_linear(pi0_ctx* ctx, const void* x, int M, int K, const void* w, int N, 
  * counterpart in the reference. For callers that must not allocate device memory after start-up
  * and may hold no pi0 context at all: a control loop with a fixed memory budget, or an embedder
  * that owns every allocation itself. Same arguments as pi0_linear plus the model dtype
- * (PI0_F16 / PI0_BF16); K must be a multiple of 32, N even.
+ * (PI0_F16 / PI0_BF16); K must be a multiple of 32, N even, x and w 16-byte aligned and y 4-byte
+ * aligned (PI0_ERR_INVALID otherwise; an out-of-range device index gives PI0_ERR_UNSUPPORTED).
+ * It always uses the engine's small-M tiling (64 × 64 tiles, split over K), which for M < 256 is
+ * exactly what pi0_linear's engine 2 runs; for M >= 256 engine 2 switches to 128 × 128 tiles
+ * without a split, so the two then agree within rounding, not bit for bit.
  * The split-K partials and tile tickets live in static device memory of this library (4 MiB of
  * fp32 partials, 4096 tiles). The first call on a device looks up their addresses and the SM
- * count with that device current (no allocation); make it before any stream capture. Returns
- * PI0_ERR_UNSUPPORTED when a call would need more scratch than that (splits·M·N > 2^20 floats or
- * more than 4096 output tiles). The tickets must be zero between calls: static memory starts
- * zeroed and every call leaves them zero. The scratch is shared by all calls on a device, so
- * calls that overlap in time (two streams or two threads) race on it and must be serialised by
- * the caller. */
+ * count with that device current; with CUDA's lazy module loading (the default) that first call,
+ * and the first call of each dtype, may also load this library's kernels and static arrays into
+ * device memory. Make one call of each dtype you use at start-up, before any stream capture;
+ * later calls allocate nothing. Returns PI0_ERR_UNSUPPORTED when a call would need more scratch
+ * than that (splits·M·N > 2^20 floats or more than 4096 output tiles). The tickets must be zero
+ * between calls: static memory starts zeroed and every call that runs alone leaves them zero.
+ * The scratch is shared by all calls on a device, so calls that overlap in time (two streams or
+ * two threads) race on it and must be serialised by the caller; one overlap can leave a ticket
+ * nonzero, after which later calls on that device give wrong results for the rest of the
+ * process. */
 int pi0_linear_noalloc(int dtype, const void* x, int M, int K, const void* w, int N, void* y,
                        pi0_stream_t stream);
 

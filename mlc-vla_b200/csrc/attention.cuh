@@ -6,9 +6,16 @@
 // Numerics follow the reference: q and k are fp32 (post-RoPE, q pre-scaled by hd^-0.5), logits
 // are accumulated in fp32 and the additive fp32 pad mask (0 / -1e9, prefix keys only) is added
 // before a fp32 softmax; probabilities are rounded to the model dtype and multiplied by the
-// model-dtype V with fp32 accumulation. q·k runs on tf32 tensor cores (cvt.rna, 10-bit
-// mantissa); the softmax is online (flash style), so probabilities are rounded before the final
-// 1/l normalisation rather than after it.
+// model-dtype V with fp32 accumulation. The q·k operands follow the reference's
+// attn_logits_dtype (gemma_dual.py:115: q and k cast to it, product accumulated in fp32):
+//   * "float32" (its default): fp32 operands, on tf32 tensor cores as three products of the
+//     split x = big + small (big = tf32(x), small = tf32(x − big)): big·big + big·small +
+//     small·big, which carries the 22-bit operand precision of fp32 accumulation (the dropped
+//     small·small term is below 2^-21 of the product);
+//   * the model dtype: q and k rounded to fp16 / bf16 first, then one tf32 product, which is
+//     exact for 16-bit operands.
+// The softmax is online (flash style), so probabilities are rounded before the final 1/l
+// normalisation rather than after it.
 //
 // Rows of one CTA tile are (t, g) pairs of one kv head: row j -> t = j / G, head = kvh·G + j % G
 // with G = H / KV, so every row of a tile shares the tile's K/V (MQA: all heads of a token).
@@ -38,7 +45,14 @@ struct AttnArgs {
   T* out;              // [B, Tq, H·hd]
   int a_is_ready;      // segment A was written before the previous kernel (the prefix cache
                        // during denoise): its tiles may be requested before griddepcontrol.wait
+  int logits_f32;      // 1: fp32 q·k operands (attn_logits_dtype "float32"); 0: model dtype
 };
+
+// tf32 operand pair (big, small) of an fp32 value: big = tf32(x), small = tf32(x − big)
+__device__ __forceinline__ void tf32_split(float x, uint32_t& big, uint32_t& small) {
+  big = to_tf32(x);
+  small = to_tf32(x - __uint_as_float(big));
+}
 
 constexpr int ATT_BQ = 64;   // query rows per CTA (4 warps × 16)
 constexpr int ATT_BK = 32;   // keys per tile
@@ -181,19 +195,39 @@ __global__ void __launch_bounds__(128) attn_kernel(AttnArgs<T> a) {
 #pragma unroll
     for (int n = 0; n < NT8; ++n) sc[n][0] = sc[n][1] = sc[n][2] = sc[n][3] = 0.f;
     const float* qw = sQ + (warp * 16) * SM::QLD;
-#pragma unroll 4
-    for (int kk = 0; kk < HD; kk += 8) {
-      uint32_t af[4];
-      af[0] = to_tf32(qw[gq * SM::QLD + kk + tq]);
-      af[1] = to_tf32(qw[(gq + 8) * SM::QLD + kk + tq]);
-      af[2] = to_tf32(qw[gq * SM::QLD + kk + tq + 4]);
-      af[3] = to_tf32(qw[(gq + 8) * SM::QLD + kk + tq + 4]);
+    if (a.logits_f32) {
+#pragma unroll 2
+      for (int kk = 0; kk < HD; kk += 8) {
+        uint32_t ab[4], as[4];
+        tf32_split(qw[gq * SM::QLD + kk + tq], ab[0], as[0]);
+        tf32_split(qw[(gq + 8) * SM::QLD + kk + tq], ab[1], as[1]);
+        tf32_split(qw[gq * SM::QLD + kk + tq + 4], ab[2], as[2]);
+        tf32_split(qw[(gq + 8) * SM::QLD + kk + tq + 4], ab[3], as[3]);
 #pragma unroll
-      for (int n = 0; n < NT8; ++n) {
-        uint32_t bf[2];
-        bf[0] = to_tf32(kt[(n * 8 + gq) * SM::KLD + kk + tq]);
-        bf[1] = to_tf32(kt[(n * 8 + gq) * SM::KLD + kk + tq + 4]);
-        mma1688_tf32(sc[n], af, bf);
+        for (int n = 0; n < NT8; ++n) {
+          uint32_t bb[2], bs[2];
+          tf32_split(kt[(n * 8 + gq) * SM::KLD + kk + tq], bb[0], bs[0]);
+          tf32_split(kt[(n * 8 + gq) * SM::KLD + kk + tq + 4], bb[1], bs[1]);
+          mma1688_tf32(sc[n], as, bb);  // small terms first
+          mma1688_tf32(sc[n], ab, bs);
+          mma1688_tf32(sc[n], ab, bb);
+        }
+      }
+    } else {
+#pragma unroll 4
+      for (int kk = 0; kk < HD; kk += 8) {
+        uint32_t af[4];  // 16-bit values are exact in tf32
+        af[0] = to_tf32(Tr<T>::r(qw[gq * SM::QLD + kk + tq]));
+        af[1] = to_tf32(Tr<T>::r(qw[(gq + 8) * SM::QLD + kk + tq]));
+        af[2] = to_tf32(Tr<T>::r(qw[gq * SM::QLD + kk + tq + 4]));
+        af[3] = to_tf32(Tr<T>::r(qw[(gq + 8) * SM::QLD + kk + tq + 4]));
+#pragma unroll
+        for (int n = 0; n < NT8; ++n) {
+          uint32_t bf[2];
+          bf[0] = to_tf32(Tr<T>::r(kt[(n * 8 + gq) * SM::KLD + kk + tq]));
+          bf[1] = to_tf32(Tr<T>::r(kt[(n * 8 + gq) * SM::KLD + kk + tq + 4]));
+          mma1688_tf32(sc[n], af, bf);
+        }
       }
     }
     // mask, online softmax

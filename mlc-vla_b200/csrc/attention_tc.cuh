@@ -24,6 +24,16 @@
 // refilled once its S MMA is done and a V slot once its P·V is done; cached prefix tiles are
 // requested before griddepcontrol.wait), warp 1 MMA issuer, warps 2-5 softmax/epilogue.
 // All waits are bounded (gemm_tc.cuh: mbar_wait).
+//
+// LO = true is the reference's default attn_logits_dtype "float32" (fp32 q·k operands,
+// gemma_dual.py:115): q and the half-scale k are split into fp16 pairs x = hi + lo with
+// hi = fp16(x) and lo = fp16(x − hi) (both written by the q/k/v epilogue, or by
+// keys_half_scale_kernel for the caller's cache), and S accumulates lo_q·hi_k + hi_q·lo_k +
+// hi_q·hi_k in fp32: 22 bits of operand precision, the dropped lo·lo term below 2^-21 of the
+// product, and a lo part that falls into the fp16 subnormal range is off by at most 2^-25 in
+// absolute terms. Q_hi stays resident; for every key tile and 64-wide head-dim block, one ring
+// stage carries that block of Q_lo (re-read from L2 per key tile), K_hi and K_lo, so shared memory
+// stays at the size of the single-product layout.
 #pragma once
 
 #include "gemm_skinny.cuh"
@@ -38,11 +48,14 @@ constexpr int KB = 64;             // keys per tile
 constexpr int NT = 192;
 constexpr float kRescale = 8.0f;   // rescale O when the row max grows by more than this
 
-template <int HD>
+template <int HD, bool LO = false>
 struct AtcSmem {
   static constexpr int NKB = HD / 64;               // 64-wide head-dim blocks
   static constexpr int Q_BYTES = 128 * HD * 2;      // NKB boxes [64 hd × 128 rows]
-  static constexpr int K_BYTES = KB * HD * 2;       // NKB boxes [64 hd × 64 keys]
+  static constexpr int QBLK = 128 * 64 * 2;         // LO: one Q_lo box
+  static constexpr int KBLK = KB * 64 * 2;          // one [64 hd × 64 keys] box
+  // K ring slot: a whole K tile (NKB boxes), or (LO) one head-dim block of Q_lo, K_hi and K_lo
+  static constexpr int K_BYTES = LO ? QBLK + 2 * KBLK : KB * HD * 2;
   static constexpr int V_BYTES = KB * HD * 2;
   static constexpr int STAGE = K_BYTES + V_BYTES;
   static constexpr int P_OFF = Q_BYTES + 2 * STAGE;
@@ -141,12 +154,15 @@ __device__ __forceinline__ void merge_rows(const AtcArgs& a, int b, int row0, in
   }
 }
 
-template <int HD>
+// tmQL / tmKAL / tmKBL: the lo parts of q and k (LO only; the hi maps otherwise, unused).
+template <int HD, bool LO>
 __global__ void __launch_bounds__(NT, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKA,
                    const __grid_constant__ CUtensorMap tmVA, const __grid_constant__ CUtensorMap tmKB,
-                   const __grid_constant__ CUtensorMap tmVB, AtcArgs a) {
-  using S = AtcSmem<HD>;
+                   const __grid_constant__ CUtensorMap tmVB, const __grid_constant__ CUtensorMap tmQL,
+                   const __grid_constant__ CUtensorMap tmKAL,
+                   const __grid_constant__ CUtensorMap tmKBL, AtcArgs a) {
+  using S = AtcSmem<HD, LO>;
   constexpr int NKB = S::NKB;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -189,6 +205,10 @@ __global__ void __launch_bounds__(NT, 1)
     tma_prefetch_desc(&tmQ);
     tma_prefetch_desc(&tmKA);
     tma_prefetch_desc(&tmVA);
+    if (LO) {
+      tma_prefetch_desc(&tmQL);
+      tma_prefetch_desc(&tmKAL);
+    }
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
@@ -214,9 +234,23 @@ __global__ void __launch_bounds__(NT, 1)
     for (int kb = 0; kb < NKB; ++kb) tma_load_2d(dst + kb * (KB * 128), m, bar, kb * 64, y);
   };
 
-  // tiles of the cached prefix do not depend on the previous kernel
+  // LO: ring stage j = (key tile j / NKB, head-dim block j % NKB) into K slot j & 1: that block
+  // of Q_lo, K_hi and K_lo
+  auto issue_lo = [&](int j) {
+    const int s = j & 1, tile = tbeg + j / NKB, kb = j % NKB;
+    const bool inA = tile < a.ntA;
+    const int y = inA ? b * a.LA + tile * KB : b * a.LB + (tile - a.ntA) * KB;
+    uint8_t* dst = sK(s);
+    mbar_expect_tx(&k_full[s], S::K_BYTES);
+    tma_load_2d(dst, &tmQL, &k_full[s], kb * 64, b * a.rows + row0);
+    tma_load_2d(dst + S::QBLK, inA ? &tmKA : &tmKB, &k_full[s], kb * 64, y);
+    tma_load_2d(dst + S::QBLK + S::KBLK, inA ? &tmKAL : &tmKBL, &k_full[s], kb * 64, y);
+  };
+
+  // tiles of the cached prefix do not depend on the previous kernel (LO: the stages also carry
+  // Q_lo, which does)
   int issued = 0;  // K and V of tiles [0, issued) requested
-  if (tid == 0 && a.a_ready)
+  if (!LO && tid == 0 && a.a_ready)
     for (; issued < min(n, 2) && tbeg + issued < a.ntA; ++issued) {
       issue(issued, false);
       issue(issued, true);
@@ -230,6 +264,32 @@ __global__ void __launch_bounds__(NT, 1)
 #pragma unroll
       for (int kb = 0; kb < NKB; ++kb)
         tma_load_2d(sQ + kb * (128 * 128), &tmQ, &q_full, kb * 64, b * a.rows + row0);
+      if constexpr (LO) {
+        int jk = 0;  // ring stages [0, jk) requested; V of tiles [0, issued)
+        for (int i = 0; i < n; ++i) {
+          bool ok = true;
+          for (int kb = 0; kb < NKB && ok; ++kb) {
+            const int j = i * NKB + kb;
+            if (j >= 2 && !mbar_wait(&k_empty[j & 1], ((j >> 1) - 1) & 1, a.err,
+                                     ERR_TIMEOUT_PRODUCER)) {
+              ok = false;
+              break;
+            }
+            issue_lo(j);
+            jk = j + 1;
+          }
+          if (!ok) break;
+          if (i >= 2 && !mbar_wait(&v_empty[i & 1], ((i >> 1) - 1) & 1, a.err, ERR_TIMEOUT_PRODUCER))
+            break;
+          issue(i, true);
+          issued = i + 1;
+        }
+        mbar_wait(&q_full, 0, a.err, ERR_TIMEOUT_PRODUCER, false);
+        for (int j = max(0, jk - 2); j < jk; ++j)
+          mbar_wait(&k_full[j & 1], (j >> 1) & 1, a.err, ERR_TIMEOUT_PRODUCER, false);
+        for (int i = max(0, issued - 2); i < issued; ++i)
+          mbar_wait(&v_full[i & 1], (i >> 1) & 1, a.err, ERR_TIMEOUT_PRODUCER, false);
+      } else {
       int issued_k = issued;  // K of tiles [0, issued_k) requested; V of [0, issued)
       for (int i = issued; i < n; ++i) {
         const uint32_t ph = ((i >> 1) - 1) & 1;
@@ -246,6 +306,7 @@ __global__ void __launch_bounds__(NT, 1)
         mbar_wait(&k_full[i & 1], (i >> 1) & 1, a.err, ERR_TIMEOUT_PRODUCER, false);
       for (int i = max(0, issued - 2); i < issued; ++i)
         mbar_wait(&v_full[i & 1], (i >> 1) & 1, a.err, ERR_TIMEOUT_PRODUCER, false);
+      }
     }
   } else if (warp == 1) {
     if (lane == 0 && n > 0) {  // MMA issuer
@@ -253,6 +314,27 @@ __global__ void __launch_bounds__(NT, 1)
       constexpr uint32_t id_o = idesc_f16<__half>(128, HD) | (1u << 16);  // B (V) MN-major
       bool ok = mbar_wait(&q_full, 0, a.err, ERR_TIMEOUT_MMA);
       auto qk = [&](int i) -> bool {
+        if constexpr (LO) {
+          for (int kb = 0; kb < NKB; ++kb) {
+            const int j = i * NKB + kb, s = j & 1;
+            if (!mbar_wait(&k_full[s], (j >> 1) & 1, a.err, ERR_TIMEOUT_MMA)) return false;
+            tc_fence_after();
+            const uint64_t dqh = desc_sw128(smem_u32(sQ + kb * (128 * 128)));
+            const uint64_t dql = desc_sw128(smem_u32(sK(s)));
+            const uint64_t dkh = desc_sw128(smem_u32(sK(s) + S::QBLK));
+            const uint64_t dkl = desc_sw128(smem_u32(sK(s) + S::QBLK + S::KBLK));
+#pragma unroll
+            for (int k = 0; k < 4; ++k)  // the small cross terms first
+              umma_f16(tmem, dql + 2 * k, dkh + 2 * k, id_s, (kb | k) != 0);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) umma_f16(tmem, dqh + 2 * k, dkl + 2 * k, id_s, 1u);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) umma_f16(tmem, dqh + 2 * k, dkh + 2 * k, id_s, 1u);
+            umma_commit(&k_empty[s]);
+          }
+          umma_commit(&s_full);
+          return true;
+        } else {
         const int s = i & 1;
         if (!mbar_wait(&k_full[s], (i >> 1) & 1, a.err, ERR_TIMEOUT_MMA)) return false;
         tc_fence_after();
@@ -266,6 +348,7 @@ __global__ void __launch_bounds__(NT, 1)
         umma_commit(&s_full);
         umma_commit(&k_empty[s]);
         return true;
+        }
       };
       auto pv = [&](int i) -> bool {
         const int s = i & 1;

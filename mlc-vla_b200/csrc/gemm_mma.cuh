@@ -217,9 +217,12 @@ struct EpiQkvRope {
   int col0;      // global column offset of this launch (skip q rows for the last prefill layer)
   float qscale;
   // tensor-core attention operands (optional): q in the model dtype instead of fp32 q, and a
-  // model-dtype copy of k at half scale next to the fp32 cache entry
+  // model-dtype copy of k at half scale next to the fp32 cache entry; for fp32 logits also their
+  // lo parts x − fp16(x) (q16lo / k16lo, set together with q16 / k16)
   T* q16 = nullptr;
   T* k16 = nullptr;
+  T* q16lo = nullptr;
+  T* k16lo = nullptr;
   __device__ void prefetch(int r, int c_local) const {
     const int c = c_local + col0;
     if (c < (H + KV) * hd) {
@@ -246,8 +249,13 @@ struct EpiQkvRope {
       if (isq) {
         const size_t qo = ((size_t)r * H + head) * hd;
         if (q16) {
-          q16[qo + i] = Tr<T>::t(__fmul_rn(o1, qscale));
-          q16[qo + i + half] = Tr<T>::t(__fmul_rn(o2, qscale));
+          const float a1 = __fmul_rn(o1, qscale), a2 = __fmul_rn(o2, qscale);
+          q16[qo + i] = Tr<T>::t(a1);
+          q16[qo + i + half] = Tr<T>::t(a2);
+          if (q16lo) {
+            q16lo[qo + i] = Tr<T>::t(a1 - Tr<T>::r(a1));
+            q16lo[qo + i + half] = Tr<T>::t(a2 - Tr<T>::r(a2));
+          }
         } else {
           q[qo + i] = __fmul_rn(o1, qscale);
           q[qo + i + half] = __fmul_rn(o2, qscale);
@@ -259,6 +267,10 @@ struct EpiQkvRope {
         if (k16) {
           k16[ko + i] = Tr<T>::t(0.5f * o1);
           k16[ko + i + half] = Tr<T>::t(0.5f * o2);
+          if (k16lo) {
+            k16lo[ko + i] = Tr<T>::t(0.5f * o1 - Tr<T>::r(0.5f * o1));
+            k16lo[ko + i + half] = Tr<T>::t(0.5f * o2 - Tr<T>::r(0.5f * o2));
+          }
         }
       }
     } else {
@@ -283,9 +295,13 @@ struct EpiQkvRope {
                              : (((size_t)b * KV + head) * T_len + pos) * hd;
       float* base = isq ? q + off : k + off;
       T* base16 = isq ? q16 : k16;
+      T* lo16 = isq ? q16lo : k16lo;
       if (!al16(cos + t) || !al16(sin + t)) return false;
       if (base16) {
         if (!al16(base16 + off + i0) || !al16(base16 + off + i0 + half)) return false;
+      }
+      if (lo16) {
+        if (!al16(lo16 + off + i0) || !al16(lo16 + off + i0 + half)) return false;
       }
       if ((!isq || !q16) && (!al16(base + i0) || !al16(base + i0 + half))) return false;
       float cs[16], sn[16];
@@ -326,6 +342,19 @@ struct EpiQkvRope {
         reinterpret_cast<uint4*>(base16 + off + i0)[1] = h1[1];
         reinterpret_cast<uint4*>(base16 + off + i0 + half)[0] = h2[0];
         reinterpret_cast<uint4*>(base16 + off + i0 + half)[1] = h2[1];
+        if (lo16) {  // the residuals x − fp16(x), exact in fp32, rounded to fp16
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float a0 = sc * o1[2 * j], a1 = sc * o1[2 * j + 1];
+            const float b0 = sc * o2[2 * j], b1 = sc * o2[2 * j + 1];
+            w1[j] = Tr<T>::pack(a0 - Tr<T>::r(a0), a1 - Tr<T>::r(a1));
+            w2[j] = Tr<T>::pack(b0 - Tr<T>::r(b0), b1 - Tr<T>::r(b1));
+          }
+          reinterpret_cast<uint4*>(lo16 + off + i0)[0] = h1[0];
+          reinterpret_cast<uint4*>(lo16 + off + i0)[1] = h1[1];
+          reinterpret_cast<uint4*>(lo16 + off + i0 + half)[0] = h2[0];
+          reinterpret_cast<uint4*>(lo16 + off + i0 + half)[1] = h2[1];
+        }
       }
     } else {
       const int cc = c0 - hq - hkv;

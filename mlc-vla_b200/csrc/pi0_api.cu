@@ -119,6 +119,10 @@ struct pi0_ctx {
   // tensor-core attention (fp16 models, one kv head): model-dtype q, and k copies at half scale
   bool attn_tc = false;
   void *q16p = nullptr, *q16s = nullptr, *kpre16 = nullptr, *ksuf16 = nullptr;
+  // fp32 attention logits (the reference's default): q·k from fp32 operands. With the tensor-core
+  // attention, the fp16 lo parts x − fp16(x) of the same q and half-scale k
+  bool logits_f32 = true;
+  void *q16p_lo = nullptr, *q16s_lo = nullptr, *kpre16_lo = nullptr, *ksuf16_lo = nullptr;
   bool pdl_barrier = false;  // the next launch waits for full completion of the previous one
   void* qscratch = nullptr;  // quantised parameters: one dequantised Linear at a time
   size_t qscratch_elems = 0;
@@ -327,6 +331,8 @@ int validate(const pi0_config& g, std::string& why) {
   if (g.ae_width > 4096 || g.vlm_width > 4096)
     return bad("expert widths above 4096 are not supported");
   if (g.action_dim > 4096) return bad("action_dim above 4096 is not supported");
+  if (g.attn_logits != PI0_LOGITS_F32 && g.attn_logits != PI0_LOGITS_MODEL_DTYPE)
+    return bad("attn_logits must be PI0_LOGITS_F32 or PI0_LOGITS_MODEL_DTYPE");
   return 0;
 }
 
@@ -646,10 +652,12 @@ int time_and_mods(pi0_ctx* ctx, const T* te, int nsteps, cudaStream_t st) {
 // many as keep the grid within one wave (at most 16, one cluster), with every split at least
 // one 64-key tile.
 template <int HD>
-int attn_tc_launch_hd(pi0_ctx* ctx, int B, const __half* q16, int rows, const __half* kA16,
-                      const __half* vA, int LA, const __half* kB16, const __half* vB, int LB,
+int attn_tc_launch_hd(pi0_ctx* ctx, int B, const __half* q16, const __half* q16lo, int rows,
+                      const __half* kA16, const __half* kA16lo, const __half* vA, int LA,
+                      const __half* kB16, const __half* kB16lo, const __half* vB, int LB,
                       const float* mask, __half* out, int a_ready, cudaStream_t st, int fam) {
-  CUtensorMap tq, tka, tva, tkb, tvb;
+  const bool lo = q16lo != nullptr;
+  CUtensorMap tq, tka, tva, tkb, tvb, tql, tkal, tkbl;
   TRY(make_tmap(ctx, &tq, q16, B * rows, HD, HD, 128, false));
   TRY(make_tmap(ctx, &tka, kA16, B * LA, HD, HD, atc::KB, false));
   TRY(make_tmap(ctx, &tva, vA, B * LA, HD, HD, atc::KB, false));
@@ -659,6 +667,16 @@ int attn_tc_launch_hd(pi0_ctx* ctx, int B, const __half* q16, int rows, const __
   } else {
     tkb = tka;
     tvb = tva;
+  }
+  if (lo) {
+    TRY(make_tmap(ctx, &tql, q16lo, B * rows, HD, HD, 128, false));
+    TRY(make_tmap(ctx, &tkal, kA16lo, B * LA, HD, HD, atc::KB, false));
+    if (LB > 0) TRY(make_tmap(ctx, &tkbl, kB16lo, B * LB, HD, HD, atc::KB, false));
+    else tkbl = tkal;
+  } else {
+    tql = tq;
+    tkal = tka;
+    tkbl = tkb;
   }
   atc::AtcArgs a{};
   a.rows = rows;
@@ -678,17 +696,24 @@ int attn_tc_launch_hd(pi0_ctx* ctx, int B, const __half* q16, int rows, const __
   a.v_lbo = atc::KB * 128;  // next 64-dim block of a V tile
   a.v_sbo = 1024;           // next 8 keys
   Prof pr(ctx, fam, st);
-  return launch(ctx, atc::attn_tc_kernel<HD>, dim3(row_tiles, splits, B), dim3(atc::NT),
-                atc::AtcSmem<HD>::BYTES, st, dim3(1, splits, 1), tq, tka, tva, tkb, tvb, a);
+  if (lo)
+    return launch(ctx, atc::attn_tc_kernel<HD, true>, dim3(row_tiles, splits, B), dim3(atc::NT),
+                  atc::AtcSmem<HD, true>::BYTES, st, dim3(1, splits, 1), tq, tka, tva, tkb, tvb,
+                  tql, tkal, tkbl, a);
+  return launch(ctx, atc::attn_tc_kernel<HD, false>, dim3(row_tiles, splits, B), dim3(atc::NT),
+                atc::AtcSmem<HD, false>::BYTES, st, dim3(1, splits, 1), tq, tka, tva, tkb, tvb,
+                tql, tkal, tkbl, a);
 }
 
-int attn_tc_launch(pi0_ctx* ctx, int B, const __half* q16, int rows, const __half* kA16,
-                   const __half* vA, int LA, const __half* kB16, const __half* vB, int LB,
+// q16lo / kA16lo / kB16lo: the fp16 lo parts for fp32 logits (null: model-dtype logits)
+int attn_tc_launch(pi0_ctx* ctx, int B, const __half* q16, const __half* q16lo, int rows,
+                   const __half* kA16, const __half* kA16lo, const __half* vA, int LA,
+                   const __half* kB16, const __half* kB16lo, const __half* vB, int LB,
                    const float* mask, __half* out, int a_ready, cudaStream_t st, int fam) {
   switch (ctx->cfg.head_dim) {
-    case 64: return attn_tc_launch_hd<64>(ctx, B, q16, rows, kA16, vA, LA, kB16, vB, LB, mask, out, a_ready, st, fam);
-    case 128: return attn_tc_launch_hd<128>(ctx, B, q16, rows, kA16, vA, LA, kB16, vB, LB, mask, out, a_ready, st, fam);
-    case 256: return attn_tc_launch_hd<256>(ctx, B, q16, rows, kA16, vA, LA, kB16, vB, LB, mask, out, a_ready, st, fam);
+    case 64: return attn_tc_launch_hd<64>(ctx, B, q16, q16lo, rows, kA16, kA16lo, vA, LA, kB16, kB16lo, vB, LB, mask, out, a_ready, st, fam);
+    case 128: return attn_tc_launch_hd<128>(ctx, B, q16, q16lo, rows, kA16, kA16lo, vA, LA, kB16, kB16lo, vB, LB, mask, out, a_ready, st, fam);
+    case 256: return attn_tc_launch_hd<256>(ctx, B, q16, q16lo, rows, kA16, kA16lo, vA, LA, kB16, kB16lo, vB, LB, mask, out, a_ready, st, fam);
   }
   return fail(ctx, PI0_ERR_UNSUPPORTED, "tensor-core attention: head_dim must be 64, 128 or 256");
 }
@@ -702,7 +727,8 @@ int convert_prefix_keys(pi0_ctx* ctx, int B, const float* keys, cudaStream_t st)
   const size_t n4 = n / 4;
   Prof pr(ctx, F_DEN_KEYS16, st);
   TRY(launch(ctx, keys_half_scale_kernel<__half>, dim3((unsigned)((n4 + 255) / 256)), dim3(256), 0,
-             st, dim3(1, 1, 1), reinterpret_cast<const float4*>(keys), (__half*)ctx->kpre16, n4));
+             st, dim3(1, 1, 1), reinterpret_cast<const float4*>(keys), (__half*)ctx->kpre16,
+             (__half*)ctx->kpre16_lo, n4));
   ctx->pdl_barrier = true;
   return 0;
 }
@@ -729,9 +755,12 @@ int run_prefill(pi0_ctx* ctx, int B, const T* prefix, const float* mask, float* 
     EpiQkvRope<T> eq{ctx->qp, kl, vl, ctx->rope_cos, ctx->rope_sin, 0, P, H, KV, hd, 0,
                      (float)std::pow((double)hd, -0.5)};
     T* k16 = ctx->attn_tc ? (T*)ctx->kpre16 + l * kv_layer : nullptr;
+    T* k16lo = ctx->kpre16_lo ? (T*)ctx->kpre16_lo + l * kv_layer : nullptr;
     if (ctx->attn_tc) {
       eq.q16 = (T*)ctx->q16p;
       eq.k16 = k16;
+      eq.q16lo = (T*)ctx->q16p_lo;
+      eq.k16lo = k16lo;
     }
     const bool last = l == g.depth - 1;
     if (last) {  // only k and v of the last layer are ever read
@@ -743,9 +772,9 @@ int run_prefill(pi0_ctx* ctx, int B, const T* prefix, const float* mask, float* 
     TRY(gemm<T>(ctx, xn, W0, (const T*)w.qkv, W0, M, hq + 2 * hkv, W0, eq, st, F_PRE_QKV));
     if constexpr (!Tr<T>::kBf16) {
       if (ctx->attn_tc) {
-        TRY(attn_tc_launch(ctx, B, (const __half*)ctx->q16p, P * H, (const __half*)k16,
-                           (const __half*)vl, P, nullptr, nullptr, 0, mask, (__half*)attn, 0, st,
-                           F_PRE_ATTN));
+        TRY(attn_tc_launch(ctx, B, (const __half*)ctx->q16p, (const __half*)ctx->q16p_lo, P * H,
+                           (const __half*)k16, (const __half*)k16lo, (const __half*)vl, P, nullptr,
+                           nullptr, nullptr, 0, mask, (__half*)attn, 0, st, F_PRE_ATTN));
         TRY(gemm<T>(ctx, attn, hq, (const T*)w.o, hq, M, W0, hq, EpiResid<T>{x, W0}, st, F_PRE_O));
         TRY(rmsnorm<T>(ctx, x, xn, M, W0, (const T*)w.ln_post, nullptr, 1, 0, st, F_PRE_NORM));
         TRY(gemm<T>(ctx, xn, W0, (const T*)w.gu, W0, M, 2 * F0, W0, EpiGeglu<T>{h, F0}, st,
@@ -767,6 +796,7 @@ int run_prefill(pi0_ctx* ctx, int B, const T* prefix, const float* mask, float* 
     a.H = H;
     a.KV = KV;
     a.out = attn;
+    a.logits_f32 = ctx->logits_f32 ? 1 : 0;
     TRY(attn_launch<T>(ctx, a, B, false, st, F_PRE_ATTN));
     TRY(gemm<T>(ctx, attn, hq, (const T*)w.o, hq, M, W0, hq, EpiResid<T>{x, W0}, st, F_PRE_O));
     TRY(rmsnorm<T>(ctx, x, xn, M, W0, (const T*)w.ln_post, nullptr, 1, 0, st, F_PRE_NORM));
@@ -814,15 +844,20 @@ int run_suffix(pi0_ctx* ctx, int B, const float* keys, const T* values, const vo
     if (ctx->attn_tc) {
       eq.q16 = (T*)ctx->q16s;
       eq.k16 = (T*)ctx->ksuf16;
+      eq.q16lo = (T*)ctx->q16s_lo;
+      eq.k16lo = (T*)ctx->ksuf16_lo;
     }
     TRY((gemm_w<T, true, false>(ctx, x, W1, (const T*)w.qkv, (const T*)w.qkv_p, w.qkv_q, M, hq + 2 * hkv,
                                 W1, eq, st, F_DEN_QKV, m_in, xn)));
     bool done_attn = false;
     if constexpr (!Tr<T>::kBf16) {
       if (ctx->attn_tc) {
-        TRY(attn_tc_launch(ctx, B, (const __half*)ctx->q16s, S * H,
-                           (const __half*)ctx->kpre16 + l * kv_layer, (const __half*)values + l * kv_layer,
-                           P, (const __half*)ctx->ksuf16, (const __half*)ctx->vsuf, S, mask,
+        const __half* kA16lo =
+            ctx->kpre16_lo ? (const __half*)ctx->kpre16_lo + l * kv_layer : nullptr;
+        TRY(attn_tc_launch(ctx, B, (const __half*)ctx->q16s, (const __half*)ctx->q16s_lo, S * H,
+                           (const __half*)ctx->kpre16 + l * kv_layer, kA16lo,
+                           (const __half*)values + l * kv_layer, P, (const __half*)ctx->ksuf16,
+                           (const __half*)ctx->ksuf16_lo, (const __half*)ctx->vsuf, S, mask,
                            (__half*)attn, 1, st, F_DEN_ATTN));
         done_attn = true;
       }
@@ -842,6 +877,7 @@ int run_suffix(pi0_ctx* ctx, int B, const float* keys, const T* values, const vo
     a.KV = KV;
     a.out = attn;
     a.a_is_ready = 1;  // the prefix K/V cache comes from prefill, not from this step
+    a.logits_f32 = ctx->logits_f32 ? 1 : 0;
     TRY(attn_launch<T>(ctx, a, B, true, st, F_DEN_ATTN));
     }
     TRY((gemm_w<T, false, true>(ctx, attn, hq, (const T*)w.o, (const T*)w.o_p, w.o_q, M, W1, hq,
@@ -935,20 +971,22 @@ int attr_attn(pi0_ctx* ctx) {
                           1));
   return 0;
 }
-template <int HD>
+template <int HD, bool LO>
 int attr_attn_tc(pi0_ctx* ctx) {
-  CK(cudaFuncSetAttribute(atc::attn_tc_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                          atc::AtcSmem<HD>::BYTES));
-  CK(cudaFuncSetAttribute(atc::attn_tc_kernel<HD>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+  CK(cudaFuncSetAttribute(atc::attn_tc_kernel<HD, LO>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                          atc::AtcSmem<HD, LO>::BYTES));
+  CK(cudaFuncSetAttribute(atc::attn_tc_kernel<HD, LO>,
+                          cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
   return 0;
 }
 template <typename T>
 int setup_attrs(pi0_ctx* ctx) {
   if (ctx->attn_tc) {
+    const bool lo = ctx->logits_f32;
     switch (ctx->cfg.head_dim) {
-      case 64: TRY(attr_attn_tc<64>(ctx)); break;
-      case 128: TRY(attr_attn_tc<128>(ctx)); break;
-      case 256: TRY(attr_attn_tc<256>(ctx)); break;
+      case 64: TRY(lo ? attr_attn_tc<64, true>(ctx) : attr_attn_tc<64, false>(ctx)); break;
+      case 128: TRY(lo ? attr_attn_tc<128, true>(ctx) : attr_attn_tc<128, false>(ctx)); break;
+      case 256: TRY(lo ? attr_attn_tc<256, true>(ctx) : attr_attn_tc<256, false>(ctx)); break;
     }
   }
   TRY(attr_gemm_both<T, EpiQkvRope<T>>(ctx));
@@ -1146,11 +1184,18 @@ int alloc_all(pi0_ctx* ctx) {
   TRY(dev_alloc(ctx, (void**)&ctx->ksuf, B * hkv * S * 4));
   TRY(dev_alloc(ctx, &ctx->vsuf, B * hkv * S * e));
   ctx->attn_tc = e == 2 && g.dtype == PI0_F16 && KV == 1 && hd % 64 == 0 && hd <= 256;
+  ctx->logits_f32 = g.attn_logits == PI0_LOGITS_F32;
   if (ctx->attn_tc) {
     TRY(dev_alloc(ctx, &ctx->q16p, MP * hq * e));
     TRY(dev_alloc(ctx, &ctx->q16s, MS * hq * e));
     TRY(dev_alloc(ctx, &ctx->kpre16, (size_t)g.depth * B * hkv * P * e));
     TRY(dev_alloc(ctx, &ctx->ksuf16, B * hkv * S * e));
+    if (ctx->logits_f32) {
+      TRY(dev_alloc(ctx, &ctx->q16p_lo, MP * hq * e));
+      TRY(dev_alloc(ctx, &ctx->q16s_lo, MS * hq * e));
+      TRY(dev_alloc(ctx, &ctx->kpre16_lo, (size_t)g.depth * B * hkv * P * e));
+      TRY(dev_alloc(ctx, &ctx->ksuf16_lo, B * hkv * S * e));
+    }
   }
   {
     const size_t kvn = (size_t)g.depth * B * KV * P * hd;
@@ -1743,7 +1788,9 @@ constexpr int kNoAllocTickets = 4096;                  // output tiles of one ca
 constexpr int kNoAllocMaxDevices = 64;
 
 // Tickets count the splits that have finished a tile; the last one resets its ticket to zero,
-// so they are zero between calls. Static device memory starts zeroed; nothing else has to.
+// so they are zero between calls that do not overlap. Static device memory starts zeroed. Two
+// calls that overlap on the GPU can leave a ticket nonzero, and then every later call that uses
+// that tile is wrong for the rest of the process: the caller must serialise the calls.
 static __device__ __align__(256) float g_noalloc_ws[kNoAllocWsFloats];
 static __device__ __align__(256) int g_noalloc_tickets[kNoAllocTickets];
 
@@ -1760,7 +1807,7 @@ std::mutex g_noalloc_mu;
 int noalloc_setup(NoAllocDev* out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return PI0_ERR_CUDA;
-  if (dev < 0 || dev >= kNoAllocMaxDevices) return PI0_ERR_DEVICE;
+  if (dev < 0 || dev >= kNoAllocMaxDevices) return PI0_ERR_UNSUPPORTED;
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
   NoAllocDev& d = g_noalloc[dev];
   if (!d.ws) {
@@ -1806,6 +1853,11 @@ int pi0_linear_noalloc(int dtype, const void* x, int M, int K, const void* w, in
                        pi0_stream_t stream) {
   if (!x || !w || !y || M < 1 || N < 2 || (N & 1) || K < 32 || (K % 32)) return PI0_ERR_INVALID;
   if (dtype != PI0_F16 && dtype != PI0_BF16) return PI0_ERR_INVALID;
+  // rows of x and w are read with 16-byte copies and y is written in pairs of elements: an
+  // offset pointer is refused here instead of faulting in the kernel
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w)) & 15 ||
+      reinterpret_cast<uintptr_t>(y) & 3)
+    return PI0_ERR_INVALID;
   NoAllocDev d;
   const int rc = noalloc_setup(&d);
   if (rc) return rc;

@@ -283,16 +283,24 @@ __global__ void div_check_kernel(const float* __restrict__ a, const float* __res
 }
 
 // Model-dtype copy of an fp32 K cache at half scale, the operand of the tensor-core attention
-// (attention_tc.cuh): k16[i] = RN(0.5·k[i]). n4 = elements / 4.
+// (attention_tc.cuh): k16[i] = RN(0.5·k[i]); for fp32 logits also the lo part
+// k16lo[i] = RN(0.5·k[i] − k16[i]) (k16lo may be null). n4 = elements / 4.
 template <typename T>
-__global__ void keys_half_scale_kernel(const float4* __restrict__ k, T* __restrict__ k16, size_t n4) {
+__global__ void keys_half_scale_kernel(const float4* __restrict__ k, T* __restrict__ k16,
+                                       T* __restrict__ k16lo, size_t n4) {
   const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n4) return;
   const float4 v = k[i];
+  const float h[4] = {0.5f * v.x, 0.5f * v.y, 0.5f * v.z, 0.5f * v.w};
   uint2 o;
-  o.x = Tr<T>::pack(0.5f * v.x, 0.5f * v.y);
-  o.y = Tr<T>::pack(0.5f * v.z, 0.5f * v.w);
+  o.x = Tr<T>::pack(h[0], h[1]);
+  o.y = Tr<T>::pack(h[2], h[3]);
   reinterpret_cast<uint2*>(k16)[i] = o;
+  if (k16lo) {
+    o.x = Tr<T>::pack(h[0] - Tr<T>::r(h[0]), h[1] - Tr<T>::r(h[1]));
+    o.y = Tr<T>::pack(h[2] - Tr<T>::r(h[2]), h[3] - Tr<T>::r(h[3]));
+    reinterpret_cast<uint2*>(k16lo)[i] = o;
+  }
 }
 
 }  // namespace pi0

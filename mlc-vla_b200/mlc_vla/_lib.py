@@ -27,6 +27,7 @@ NVCC_FLAGS = [
 PI0_OK, PI0_ERR_INVALID, PI0_ERR_CUDA, PI0_ERR_NO_PARAMS, PI0_ERR_DEVICE, PI0_ERR_UNSUPPORTED = range(6)
 PI0_F16, PI0_BF16, PI0_F32, PI0_U32 = range(4)
 PI0_QUANT_NONE, PI0_QUANT_Q4, PI0_QUANT_Q3 = range(3)
+PI0_LOGITS_F32, PI0_LOGITS_MODEL_DTYPE = range(2)
 
 DTYPE_CODE = {"float16": PI0_F16, "bfloat16": PI0_BF16, "float32": PI0_F32, "uint32": PI0_U32}
 CODE_DTYPE = {v: k for k, v in DTYPE_CODE.items()}
@@ -79,6 +80,7 @@ class Pi0ConfigC(ctypes.Structure):
         ("action_dim", ctypes.c_int32), ("num_denoise_steps", ctypes.c_int32),
         ("dtype", ctypes.c_int32), ("quant", ctypes.c_int32), ("max_batch", ctypes.c_int32),
         ("rms_norm_eps", ctypes.c_float), ("rope_theta", ctypes.c_float),
+        ("attn_logits", ctypes.c_int32),
     ]
 
 

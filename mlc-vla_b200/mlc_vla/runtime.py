@@ -94,13 +94,24 @@ def config_struct(cfg: Pi0Config, max_batch: int = 1, quant=None) -> _lib.Pi0Con
     qcode = _lib.PI0_QUANT_NONE
     if quant is not None:
         qcode = _lib.PI0_QUANT_Q3 if quant.quantize_dtype == "int3" else _lib.PI0_QUANT_Q4
+    # attention logits operands (gemma_dual.py:115): fp32 (the reference's default) or the model
+    # dtype; the reference would cast to any dtype, this build implements these two
+    logits = getattr(cfg, "attn_logits_dtype", "float32")
+    if logits == "float32":
+        lcode = _lib.PI0_LOGITS_F32
+    elif logits == dtype:
+        lcode = _lib.PI0_LOGITS_MODEL_DTYPE
+    else:
+        raise ValueError(
+            f"attn_logits_dtype={logits!r}: the B200 build computes the attention logits from "
+            f"float32 or model-dtype ({dtype}) operands")
     return _lib.Pi0ConfigC(
         vlm_width=vlm.width, vlm_mlp_dim=vlm.mlp_dim, ae_width=ae.width, ae_mlp_dim=ae.mlp_dim,
         depth=vlm.depth, num_heads=vlm.num_heads, num_kv_heads=vlm.num_kv_heads,
         head_dim=vlm.head_dim, prefix_len=cfg.prefix_len, action_horizon=cfg.action_horizon,
         action_dim=cfg.action_dim, num_denoise_steps=cfg.num_denoise_steps,
         dtype=_lib.DTYPE_CODE[dtype], quant=qcode, max_batch=max_batch,
-        rms_norm_eps=cfg.rms_norm_eps, rope_theta=cfg.rope_theta)
+        rms_norm_eps=cfg.rms_norm_eps, rope_theta=cfg.rope_theta, attn_logits=lcode)
 
 
 class Pi0Runtime:

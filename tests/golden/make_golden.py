@@ -2,7 +2,9 @@
 
 Run here (where the read-only reference checkout exists), never on the GPU box:
 
-    python tests/golden/make_golden.py [--reference /path/to/mlc-vla]
+    python tests/golden/make_golden.py --reference /path/to/mlc-vla
+
+(or set MLC_VLA_REFERENCE to the reference checkout instead of passing --reference)
 
 What it does:
 
@@ -126,9 +128,12 @@ def write_loader_map(ref):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("MLC_VLA_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("MLC_VLA_REFERENCE"),
+                    help="the reference checkout (default: $MLC_VLA_REFERENCE)")
     ap.add_argument("--loader-map-only", action="store_true")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("give --reference or set MLC_VLA_REFERENCE")
 
     ref = load_reference(args.reference)
     sys.path.insert(0, os.path.join(REPO, "mlc-vla_b200"))

@@ -30,3 +30,25 @@ def inputs(cfg, seed=1, batch=1):
     noise = rng.standard_normal((batch, cfg.action_horizon, cfg.action_dim)).astype(np.float32)
     te = sinusoidal_time_emb(0.7, cfg.action_expert.width)
     return {"prefix": prefix, "x_t": x_t, "time_emb": te, "noise": noise}
+
+
+def seeded_weights(named_params, seed=0, scale=0.02, threads=None):
+    """N(0, scale²) fp32 weights in parameter-table order, fast enough for the 2.4 B-parameter
+    π0.5 model: entry i is drawn from its own ``default_rng([seed, i])`` (float32 normals), so
+    the values do not depend on the number of threads that draw them. Integer entries are
+    zeros."""
+    from concurrent.futures import ThreadPoolExecutor
+    import os
+
+    def draw(item):
+        i, (_, spec) = item
+        shape = tuple(int(s) for s in spec.shape)
+        if str(spec.dtype).startswith(("int", "uint")):
+            return np.zeros(shape, spec.dtype)
+        w = np.random.default_rng([seed, i]).standard_normal(shape, dtype=np.float32)
+        w *= np.float32(scale)
+        return w
+
+    with ThreadPoolExecutor(threads or os.cpu_count() or 1) as ex:
+        vals = list(ex.map(draw, enumerate(named_params)))
+    return {name: v for (name, _), v in zip(named_params, vals)}

@@ -278,3 +278,33 @@ def test_m0_equals_m1_full_width():
     ko, vo = m.oracle_kv(inp["prefix"], pm)
     vref = O.denoise_step_kv(m.p, cfg, ko, vo, inp["x_t"], inp["time_emb"], sc, ss, pm)
     _check(v0, vref, what="M0 full width vs oracle")
+
+
+@pytest.mark.parametrize("kw,dtype,logits", [
+    (recipes.MINI, "float16", "float16"), (recipes.MINI, "bfloat16", "bfloat16"),
+    (recipes.DUMMY, "float16", "float16"), (recipes.FULL2, "float16", "float16")])
+def test_model_dtype_logits_match_oracle(kw, dtype, logits):
+    """attn_logits_dtype set to the model dtype (the reference's tensor-core option,
+    pi0_config.py:97-102, gemma_dual.py:115: q and k cast to fp16 / bf16 before q·kᵀ) against
+    the oracle computing the same cast; the default "float32" is what every other test runs."""
+    m = Model(config(kw, dtype, attn_logits_dtype=logits))
+    cfg = m.cfg
+    inp = m.inputs()
+    pm = O.prefix_mask(cfg.prefix_len)
+    sc, ss = O.suffix_rope(cfg, cfg.prefix_len)
+    te = O.time_embs(cfg.num_denoise_steps, cfg.action_expert.width)
+    k, v = m.rt.prefill(inp["prefix"], pm)
+    ko, vo = m.oracle_kv(inp["prefix"], pm)
+    _check(_np(k), ko, 0.99999, 1e-2 * np.abs(ko).max(), f"{logits} logits keys")
+    x = _np(m.rt.denoise_loop_kv(k, v, inp["noise"], te, sc, ss, pm))
+    xo = O.denoise_loop_kv(m.p, cfg, ko, vo, inp["noise"], te, sc, ss, pm)
+    tol = MAXABS if dtype == "float16" else 8e-2
+    _check(x, xo, 0.999 if dtype == "bfloat16" else COS, tol,
+           f"{kw['paligemma_variant']} {dtype} {logits} logits")
+
+
+def test_unsupported_logits_dtype_is_refused():
+    from mlc_vla.runtime import Pi0Runtime
+
+    with pytest.raises(ValueError, match="attn_logits_dtype"):
+        Pi0Runtime(config(recipes.MINI, "float16", attn_logits_dtype="bfloat16"), device=0)
