@@ -61,8 +61,15 @@ struct AtcSmem {
   static constexpr int P_OFF = Q_BYTES + 2 * STAGE;
   static constexpr int P_BYTES = 128 * KB * 2;      // [128 rows × 64 keys] fp16
   static constexpr int LOAD = P_OFF + P_BYTES;
-  static constexpr int OLD = HD + 4;                // merge buffer row stride (floats)
-  static constexpr int MERGE = 128 * OLD * 4 + 128 * 8;
+  // key-split merge (after the key loop, aliasing the loop buffers): this CTA's partial as
+  // normalised fp16 rows O/l [128][HD] and fp32 (m, l) [128][2], then the received row blocks of
+  // every split: [splits][rpr][HD] fp16 and [splits][rpr][2] fp32, rpr·splits ≤ 160 rows (≤ 16
+  // splits, rpr = ⌈128 / splits⌉ rounded up to even)
+  static constexpr int P16 = 128 * HD * 2;
+  static constexpr int PML = P16;                   // + 128·8
+  static constexpr int R16 = PML + 1024;            // + 160·HD·2
+  static constexpr int RML = R16 + 160 * HD * 2;    // + 160·8
+  static constexpr int MERGE = RML + 160 * 8;
   static constexpr int BYTES = (LOAD > MERGE ? LOAD : MERGE) + 1024;
 };
 
@@ -75,6 +82,7 @@ struct AtcArgs {
   void* out;          // [B·rows, HD] fp16
   int* err;
   int a_ready;        // segment A was written before the previous kernel
+  int ya0;            // row of segment A's first key in its tensor map (layer offset)
   uint32_t v_lbo, v_sbo;  // MN-major V descriptor: byte stride between 64-dim blocks / 8-key groups
 };
 
@@ -102,131 +110,85 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       : "memory");
 }
 
-// Final rows [rbeg, rend) of a row tile from the nsplit ≤ NSB key-split partials (unnormalised O
-// at `oaddr` in every rank's shared memory, row stride OLD floats; merge weights s_w, 1 / Σ w·l in
-// s_inv): one item = (row, 4 dims); a thread takes G = 32 / NSB items per pass and issues the
-// G·nsplit cluster loads of all of them together, so a pass costs one round trip over the
-// cluster. The partials of an item are summed in rank order.
-template <int HD, int NSB>
-__device__ __forceinline__ void merge_rows(const AtcArgs& a, int b, int row0, int rbeg, int rend,
-                                           int nsplit, uint32_t oaddr, float (*s_w)[16],
-                                           const float* s_inv, int tid) {
-  constexpr int G = 32 / NSB, OLD = AtcSmem<HD>::OLD;
-  const int items = (rend - rbeg) * (HD / 4);
-#pragma unroll 1
-  for (int it0 = tid; it0 < items; it0 += G * NT) {
-    float4 v[G][NSB];
-#pragma unroll
-    for (int j = 0; j < G; ++j) {
-      const int it = it0 + j * NT;
-      if (it < items) {
-        const int rr = it / (HD / 4), d = (it % (HD / 4)) * 4;
-        const uint32_t off = oaddr + ((rbeg + rr) * OLD + d) * 4;
-#pragma unroll
-        for (int c = 0; c < NSB; ++c)
-          if (c < nsplit) v[j][c] = ld_cluster4(map_rank(off, c));
-      }
-    }
-#pragma unroll
-    for (int j = 0; j < G; ++j) {
-      const int it = it0 + j * NT;
-      if (it < items) {
-        const int rr = it / (HD / 4), d = (it % (HD / 4)) * 4;
-        const int row = row0 + rbeg + rr;
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-        for (int c = 0; c < NSB; ++c)
-          if (c < nsplit) {
-            const float w = s_w[rr][c];
-            acc.x += w * v[j][c].x;
-            acc.y += w * v[j][c].y;
-            acc.z += w * v[j][c].z;
-            acc.w += w * v[j][c].w;
-          }
-        if (row < a.rows) {
-          const float inv = s_inv[rr];
-          __half* out = reinterpret_cast<__half*>(a.out) + ((size_t)b * a.rows + row) * HD + d;
-          *reinterpret_cast<uint2*>(out) = make_uint2(Tr<__half>::pack(acc.x * inv, acc.y * inv),
-                                                      Tr<__half>::pack(acc.z * inv, acc.w * inv));
-        }
-      }
-    }
+// Barriers and small buffers of one attention CTA (static shared memory of the calling kernel).
+struct AtcShared {
+  uint64_t q_full, k_full[2], k_empty[2], v_full[2], v_empty[2], s_full, s_free, p_full, pv_done,
+      drain, recv;
+  float mask[KB];
+  float w[128][16];
+  float inv[128];
+};
+
+// One thread: initialise the barriers (before the CTA-wide barrier that precedes attn_tile).
+__device__ __forceinline__ void atc_init(AtcShared& sm) {
+  mbar_init(&sm.q_full, 1);
+  for (int s = 0; s < 2; ++s) {
+    mbar_init(&sm.k_full[s], 1);
+    mbar_init(&sm.k_empty[s], 1);
+    mbar_init(&sm.v_full[s], 1);
+    mbar_init(&sm.v_empty[s], 1);
   }
+  mbar_init(&sm.s_full, 1);
+  mbar_init(&sm.s_free, 4);
+  mbar_init(&sm.p_full, 4);
+  mbar_init(&sm.pv_done, 1);
+  mbar_init(&sm.drain, 1);
+  mbar_init(&sm.recv, 1);
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
 
-// tmQL / tmKAL / tmKBL: the lo parts of q and k (LO only; the hi maps otherwise, unused).
+// One thread: invalidate the barriers of a finished attn_tile (no copy or MMA is pending on them)
+// before atc_init makes them fresh for the next one.
+__device__ __forceinline__ void atc_inval(AtcShared& sm) {
+  uint64_t* b[15] = {&sm.q_full, &sm.k_full[0], &sm.k_full[1], &sm.k_empty[0], &sm.k_empty[1],
+                     &sm.v_full[0], &sm.v_full[1], &sm.v_empty[0], &sm.v_empty[1], &sm.s_full,
+                     &sm.s_free, &sm.p_full, &sm.pv_done, &sm.drain, &sm.recv};
+#pragma unroll
+  for (int i = 0; i < 15; ++i)
+    asm volatile("mbarrier.inval.shared::cta.b64 [%0];" ::"r"(smem_u32(b[i])) : "memory");
+}
+
+// The work of one CTA: query rows [row0, row0 + 128) of batch element b against key tiles
+// [tbeg, tbeg + n), split `rank` of `nsplit` (the splits of a row tile are consecutive cluster
+// ranks and are merged here when nsplit > 1; every rank of the cluster calls this). TMEM: S in
+// columns [0, 64), O in [256, 256 + HD) of `tmem` (512 columns). pdl: called from a kernel
+// launched with programmatic dependent launch (cached prefix tiles are requested before its
+// griddepcontrol.wait). tmQL / tmKAL / tmKBL: the lo parts of q and k (LO only).
 template <int HD, bool LO>
-__global__ void __launch_bounds__(NT, 1)
-    attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKA,
-                   const __grid_constant__ CUtensorMap tmVA, const __grid_constant__ CUtensorMap tmKB,
-                   const __grid_constant__ CUtensorMap tmVB, const __grid_constant__ CUtensorMap tmQL,
-                   const __grid_constant__ CUtensorMap tmKAL,
-                   const __grid_constant__ CUtensorMap tmKBL, AtcArgs a) {
+__device__ __forceinline__ void attn_tile(const CUtensorMap& tmQ, const CUtensorMap& tmKA,
+                                          const CUtensorMap& tmVA, const CUtensorMap& tmKB,
+                                          const CUtensorMap& tmVB, const CUtensorMap& tmQL,
+                                          const CUtensorMap& tmKAL, const CUtensorMap& tmKBL,
+                                          const AtcArgs& a, int b, int row0, int tbeg, int n,
+                                          int nsplit, uint32_t rank, uint8_t* base,
+                                          AtcShared& sm, uint32_t tmem, bool pdl) {
   using S = AtcSmem<HD, LO>;
   constexpr int NKB = S::NKB;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~static_cast<uintptr_t>(1023));
-  // K and V tiles travel in separate two-slot rings: a K slot is free once its S = Q·Kᵀ is done,
-  // a V slot once its O += P·V is done, so the next K tiles do not wait for the P·V chain
-  __shared__ __align__(8) uint64_t q_full, k_full[2], k_empty[2], v_full[2], v_empty[2], s_full,
-      s_free, p_full, pv_done, drain;
-  __shared__ uint32_t s_tmem;
-  __shared__ float s_mask[KB];
-  __shared__ float s_w[128][16];
-  __shared__ float s_inv[128];
-
+  uint64_t& q_full = sm.q_full;
+  uint64_t* k_full = sm.k_full;
+  uint64_t* k_empty = sm.k_empty;
+  uint64_t* v_full = sm.v_full;
+  uint64_t* v_empty = sm.v_empty;
+  uint64_t& s_full = sm.s_full;
+  uint64_t& s_free = sm.s_free;
+  uint64_t& p_full = sm.p_full;
+  uint64_t& pv_done = sm.pv_done;
+  uint64_t& drain = sm.drain;
+  float* s_mask = sm.mask;
+  float(*s_w)[16] = sm.w;
+  float* s_inv = sm.inv;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int b = blockIdx.z;
-  const int row0 = blockIdx.x * 128;
-  const int nsplit = gridDim.y;
-  const uint32_t rank = cluster_rank();
-  const int tbeg = blockIdx.y * a.tps;
-  const int n = max(0, min(a.nt, tbeg + a.tps) - tbeg);
   uint8_t* sQ = base;
   uint8_t* sP = base + S::P_OFF;
   auto sK = [&](int s) { return base + S::Q_BYTES + s * S::STAGE; };
   auto sV = [&](int s) { return base + S::Q_BYTES + s * S::STAGE + S::K_BYTES; };
-
-  if (tid == 0) {
-    mbar_init(&q_full, 1);
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(&k_full[s], 1);
-      mbar_init(&k_empty[s], 1);
-      mbar_init(&v_full[s], 1);
-      mbar_init(&v_empty[s], 1);
-    }
-    mbar_init(&s_full, 1);
-    mbar_init(&s_free, 4);
-    mbar_init(&p_full, 4);
-    mbar_init(&pv_done, 1);
-    mbar_init(&drain, 1);
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    tma_prefetch_desc(&tmQ);
-    tma_prefetch_desc(&tmKA);
-    tma_prefetch_desc(&tmVA);
-    if (LO) {
-      tma_prefetch_desc(&tmQL);
-      tma_prefetch_desc(&tmKAL);
-    }
-  }
-  if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                     smem_u32(&s_tmem)),
-                 "r"(512u));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = s_tmem;  // S: columns [0, 64); O: columns [256, 256 + HD)
 
   // one K (is_v = false) or V tile of key tile i into ring slot i & 1
   auto issue = [&](int i, bool is_v) {
     const int s = i & 1, tile = tbeg + i;
     const bool inA = tile < a.ntA;
     const CUtensorMap* m = inA ? (is_v ? &tmVA : &tmKA) : (is_v ? &tmVB : &tmKB);
-    const int y = inA ? b * a.LA + tile * KB : b * a.LB + (tile - a.ntA) * KB;
+    const int y = inA ? a.ya0 + b * a.LA + tile * KB : b * a.LB + (tile - a.ntA) * KB;
     uint64_t* bar = is_v ? &v_full[s] : &k_full[s];
     uint8_t* dst = is_v ? sV(s) : sK(s);
     mbar_expect_tx(bar, is_v ? S::V_BYTES : S::K_BYTES);
@@ -239,7 +201,7 @@ __global__ void __launch_bounds__(NT, 1)
   auto issue_lo = [&](int j) {
     const int s = j & 1, tile = tbeg + j / NKB, kb = j % NKB;
     const bool inA = tile < a.ntA;
-    const int y = inA ? b * a.LA + tile * KB : b * a.LB + (tile - a.ntA) * KB;
+    const int y = inA ? a.ya0 + b * a.LA + tile * KB : b * a.LB + (tile - a.ntA) * KB;
     uint8_t* dst = sK(s);
     mbar_expect_tx(&k_full[s], S::K_BYTES);
     tma_load_2d(dst, &tmQL, &k_full[s], kb * 64, b * a.rows + row0);
@@ -250,13 +212,15 @@ __global__ void __launch_bounds__(NT, 1)
   // tiles of the cached prefix do not depend on the previous kernel (LO: the stages also carry
   // Q_lo, which does)
   int issued = 0;  // K and V of tiles [0, issued) requested
-  if (!LO && tid == 0 && a.a_ready)
+  if (!LO && pdl && tid == 0 && a.a_ready)
     for (; issued < min(n, 2) && tbeg + issued < a.ntA; ++issued) {
       issue(issued, false);
       issue(issued, true);
     }
-  pdl_trigger();
-  pdl_wait();
+  if (pdl) {
+    pdl_trigger();
+    pdl_wait();
+  }
 
   if (warp == 0) {
     if (lane == 0) {  // producer
@@ -488,65 +452,152 @@ __global__ void __launch_bounds__(NT, 1)
           for (int u = 0; u < 4; ++u) reinterpret_cast<uint4*>(out + c)[u] = pk[u];
       }
     } else {
-      // partial (m, l, unnormalised O) of this split into shared memory for the merge
-      float* sO = reinterpret_cast<float*>(base);
-      float* sML = sO + 128 * S::OLD;
+      // partial of this split for the merge: the row normalised by its own sum, O / l, in fp16
+      // (bounded by max |v|, so no overflow), and (m, l) in fp32
+      __half* sO = reinterpret_cast<__half*>(base);
+      float* sML = reinterpret_cast<float*>(base + S::PML);
+      const float inv = have && l > 0.f ? 1.f / l : 0.f;
 #pragma unroll 1
       for (int c = 0; c < HD; c += 32) {
         uint32_t ov[32];
         if (have) tmem_ld32(tO + c, ov);
+        uint4 pk[4];
+        uint32_t* pw = reinterpret_cast<uint32_t*>(pk);
 #pragma unroll
-        for (int u = 0; u < 8; ++u)
-          *reinterpret_cast<float4*>(sO + r * S::OLD + c + 4 * u) =
-              have ? make_float4(__uint_as_float(ov[4 * u]), __uint_as_float(ov[4 * u + 1]),
-                                 __uint_as_float(ov[4 * u + 2]), __uint_as_float(ov[4 * u + 3]))
-                   : make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int h = 0; h < 16; ++h)
+          pw[h] = have ? Tr<__half>::pack(__uint_as_float(ov[2 * h]) * inv,
+                                          __uint_as_float(ov[2 * h + 1]) * inv)
+                       : 0u;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) reinterpret_cast<uint4*>(sO + r * HD + c)[u] = pk[u];
       }
-      sML[2 * r] = have ? m_ref : -1e30f;
+      sML[2 * r] = have && l > 0.f ? m_ref : -1e30f;
       sML[2 * r + 1] = have ? l : 0.f;
     }
   }
 
   if (nsplit > 1) {
     // ---- merge the key splits of this row tile: rank r finishes rows [r·rpr, (r+1)·rpr) ----
+    // Every split pushes its normalised partial rows of rank r's block (one bulk copy for O, one
+    // for (m, l)) into rank r's receive buffer, completing on rank r's `recv` barrier; rank r then
+    // merges from its own shared memory: out = Σ_s c_s·o_s with c_s = e^(m_s − M)·l_s / Σ e^(m − M)·l,
+    // summed in split order.
+    const int rpr = ((128 + nsplit - 1) / nsplit + 1) & ~1;  // even: 16-byte (m, l) blocks
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     tc_fence_before();
-    cluster_sync();
-    const float* sO = reinterpret_cast<const float*>(base);
-    const float* sML = sO + 128 * S::OLD;
-    const uint32_t maddr = smem_u32(sML);
-    const int rpr = (128 + nsplit - 1) / nsplit;
-    const int rbeg = rank * rpr, rend = min(128, rbeg + rpr);
-    for (int rr = tid; rr < rend - rbeg; rr += NT) {
-      const int row = rbeg + rr;
-      float mm[16], ll[16];
+    __syncthreads();
+    cluster_sync();  // every split's partial is written and its loop buffers are free
+    const __half* sO = reinterpret_cast<const __half*>(base);
+    const float* sML = reinterpret_cast<const float*>(base + S::PML);
+    __half* rO = reinterpret_cast<__half*>(base + S::R16);
+    float* rML = reinterpret_cast<float*>(base + S::RML);
+    if ((int)rank < nsplit && tid < nsplit) {  // split `rank`, thread t: rank t's row block
+      const int r0 = tid * rpr, nr = max(0, min(128, r0 + rpr) - r0);
+      if (nr > 0) {
+        const uint32_t mb = map_rank(smem_u32(&sm.recv), (uint32_t)tid);
+        const uint32_t dO = map_rank(smem_u32(rO + (size_t)rank * rpr * HD), (uint32_t)tid);
+        const uint32_t dM = map_rank(smem_u32(rML + (size_t)rank * rpr * 2), (uint32_t)tid);
+        asm volatile(
+            "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dO),
+            "r"(smem_u32(sO + (size_t)r0 * HD)), "r"((uint32_t)(nr * HD * 2)), "r"(mb)
+            : "memory");
+        asm volatile(
+            "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dM),
+            "r"(smem_u32(sML + (size_t)r0 * 2)), "r"((uint32_t)(nr * 8)), "r"(mb)
+            : "memory");
+      }
+      asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+    }
+    const int rbeg = (int)rank * rpr, rend = min(128, rbeg + rpr), nme = max(0, rend - rbeg);
+    if ((int)rank < nsplit && nme > 0) {
+      if (tid == 0) {
+        mbar_expect_tx(&sm.recv, (uint32_t)(nsplit * nme * (HD * 2 + 8)));
+        mbar_wait(&sm.recv, 0, a.err, ERR_TIMEOUT_EPI, false);
+      }
+      __syncthreads();
+      for (int rr = tid; rr < nme; rr += NT) {  // merge coefficients of row rbeg + rr
+        float mm[16], ll[16];
+        float M = -1e30f;
 #pragma unroll
-      for (int c = 0; c < 16; ++c) {
-        mm[c] = -1e30f;
-        ll[c] = 0.f;
-        if (c < nsplit) {
-          const float4 v = ld_cluster4(map_rank(maddr + (row & ~1) * 8, c));
-          mm[c] = (row & 1) ? v.z : v.x;
-          ll[c] = (row & 1) ? v.w : v.y;
+        for (int c = 0; c < 16; ++c) {
+          mm[c] = c < nsplit ? rML[((size_t)c * rpr + rr) * 2] : -1e30f;
+          ll[c] = c < nsplit ? rML[((size_t)c * rpr + rr) * 2 + 1] : 0.f;
+          M = fmaxf(M, mm[c]);
+        }
+        float L = 0.f;
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+          const float w = c < nsplit ? expf(mm[c] - M) * ll[c] : 0.f;
+          s_w[rr][c] = w;
+          L += w;
+        }
+        s_inv[rr] = L > 0.f ? 1.f / L : 0.f;
+      }
+      __syncthreads();
+      const int items = nme * (HD / 8);
+      for (int it = tid; it < items; it += NT) {  // (row, 8 dims)
+        const int rr = it / (HD / 8), d = (it % (HD / 8)) * 8;
+        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        for (int c = 0; c < nsplit; ++c) {
+          const uint4 v = *reinterpret_cast<const uint4*>(rO + ((size_t)c * rpr + rr) * HD + d);
+          const __half* e = reinterpret_cast<const __half*>(&v);
+          const float wc = s_w[rr][c] * s_inv[rr];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) acc[j] += wc * __half2float(e[j]);
+        }
+        const int row = row0 + rbeg + rr;
+        if (row < a.rows) {
+          uint4 o;
+          uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) ow[j] = Tr<__half>::pack(acc[2 * j], acc[2 * j + 1]);
+          *reinterpret_cast<uint4*>(reinterpret_cast<__half*>(a.out) + ((size_t)b * a.rows + row) * HD + d) = o;
         }
       }
-      float M = -1e30f;
-#pragma unroll
-      for (int c = 0; c < 16; ++c) M = fmaxf(M, mm[c]);
-      float L = 0.f;
-#pragma unroll
-      for (int c = 0; c < 16; ++c) {
-        const float w = c < nsplit ? expf(mm[c] - M) : 0.f;
-        s_w[rr][c] = w;
-        L += w * ll[c];
-      }
-      s_inv[rr] = L > 0.f ? 1.f / L : 0.f;
     }
+    if ((int)rank < nsplit && tid < nsplit) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
     __syncthreads();
-    if (nsplit <= 4) merge_rows<HD, 4>(a, b, row0, rbeg, rend, nsplit, smem_u32(sO), s_w, s_inv, tid);
-    else if (nsplit <= 8) merge_rows<HD, 8>(a, b, row0, rbeg, rend, nsplit, smem_u32(sO), s_w, s_inv, tid);
-    else merge_rows<HD, 16>(a, b, row0, rbeg, rend, nsplit, smem_u32(sO), s_w, s_inv, tid);
-    cluster_sync();  // peers may still read this CTA's partial
   }
+}
+
+// tmQL / tmKAL / tmKBL: the lo parts of q and k (LO only; the hi maps otherwise, unused).
+template <int HD, bool LO>
+__global__ void __launch_bounds__(NT, 1)
+    attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKA,
+                   const __grid_constant__ CUtensorMap tmVA, const __grid_constant__ CUtensorMap tmKB,
+                   const __grid_constant__ CUtensorMap tmVB, const __grid_constant__ CUtensorMap tmQL,
+                   const __grid_constant__ CUtensorMap tmKAL,
+                   const __grid_constant__ CUtensorMap tmKBL, AtcArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  __shared__ AtcShared sm;
+  __shared__ uint32_t s_tmem;
+  const int tid = threadIdx.x, warp = tid >> 5;
+  if (tid == 0) {
+    atc_init(sm);
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmKA);
+    tma_prefetch_desc(&tmVA);
+    if (LO) {
+      tma_prefetch_desc(&tmQL);
+      tma_prefetch_desc(&tmKAL);
+    }
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(&s_tmem)),
+                 "r"(512u));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s_tmem;
+  const int tbeg = blockIdx.y * a.tps;
+  const int n = max(0, min(a.nt, tbeg + a.tps) - tbeg);
+  attn_tile<HD, LO>(tmQ, tmKA, tmVA, tmKB, tmVB, tmQL, tmKAL, tmKBL, a, blockIdx.z,
+                    blockIdx.x * 128, tbeg, n, gridDim.y, cluster_rank(), base, sm, tmem, true);
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {

@@ -14,6 +14,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -31,6 +32,7 @@
 #include "gemm_tc.cuh"
 #include "gemm_skinny.cuh"
 #include "small_kernels.cuh"
+#include "denoise_step.cuh"
 
 using namespace pi0;
 
@@ -124,6 +126,16 @@ struct pi0_ctx {
   bool logits_f32 = true;
   void *q16p_lo = nullptr, *q16s_lo = nullptr, *kpre16_lo = nullptr, *ksuf16_lo = nullptr;
   bool pdl_barrier = false;  // the next launch waits for full completion of the previous one
+  // persistent denoise step (denoise_step.cuh): batch-1 fp16 π0.5-width models
+  bool step_kernel = false;
+  int step_grid = 0;
+  ds::Work* step_plan = nullptr;    // [G_NUM][step_grid]
+  ds::Layer* step_layers = nullptr; // [depth]
+  unsigned long long* step_bar = nullptr;  // grid barrier word
+  int step_tiles[ds::G_NUM] = {}, step_nkb[ds::G_NUM] = {}, step_N[ds::G_NUM] = {},
+      step_K[ds::G_NUM] = {};
+  int att_row_tiles = 0, att_tps = 0, att_splits = 0, att_ntA = 0, att_nt = 0;
+  std::string step_why;             // why the persistent step is not used (empty: it is)
   void* qscratch = nullptr;  // quantised parameters: one dequantised Linear at a time
   size_t qscratch_elems = 0;
   void *t1 = nullptr, *cond = nullptr, *mods = nullptr;
@@ -157,14 +169,15 @@ namespace {
 enum Fam {
   F_PRE_NORM, F_PRE_QKV, F_PRE_ATTN, F_PRE_O, F_PRE_GU, F_PRE_DOWN,
   F_DEN_TIME_MODS, F_DEN_ACT_IN, F_DEN_NORM, F_DEN_QKV, F_DEN_ATTN, F_DEN_O, F_DEN_GU,
-  F_DEN_DOWN, F_DEN_ACT_OUT, F_DEN_KEYS16, F_NUM
+  F_DEN_DOWN, F_DEN_ACT_OUT, F_DEN_KEYS16, F_DEN_STEP, F_NUM
 };
 const char* kFamName[F_NUM] = {
   "prefill.rmsnorm", "prefill.qkv_rope_gemm", "prefill.attention", "prefill.o_gemm",
   "prefill.gate_up_geglu_gemm", "prefill.down_gemm",
   "denoise.time_mlp_modulation_gemm", "denoise.action_in", "denoise.ada_rmsnorm",
   "denoise.qkv_rope_gemm", "denoise.attention", "denoise.o_gemm", "denoise.gate_up_geglu_gemm",
-  "denoise.down_gemm", "denoise.action_out_euler", "denoise.prefix_keys_fp16"};
+  "denoise.down_gemm", "denoise.action_out_euler", "denoise.prefix_keys_fp16",
+  "denoise.step_persistent"};
 
 int fail(pi0_ctx* c, int code, const std::string& msg) {
   if (c) c->err = msg;
@@ -733,6 +746,220 @@ int convert_prefix_keys(pi0_ctx* ctx, int B, const float* keys, cudaStream_t st)
   return 0;
 }
 
+// ---- persistent denoise step ---------------------------------------------------------------
+// Work plan of one GEMM phase over `grid` CTAs in clusters of ds::CL (denoise_step.cuh): every
+// 128-row weight tile gets a split group of s ranks, s the largest power of two ≤ 8 with
+// tiles·s ≤ grid, and (unless `uniform`) tiles are promoted to 2s while CTAs are left; groups are
+// packed into clusters largest first (power-of-two sizes, so a group never straddles a cluster
+// and its first rank is a multiple of its size). Rank j of a group takes k-blocks
+// [j·⌈nkb/s⌉, (j+1)·⌈nkb/s⌉). Returns false when no plan exists.
+bool step_gemm_plan(int grid, int tiles, int nkb, bool uniform, ds::Work* out, int* s_out) {
+  int smax = 0;
+  for (int sz = ds::CL; sz >= 1; sz >>= 1)
+    if (tiles * sz <= grid) {
+      smax = sz;
+      break;
+    }
+  if (!smax) return false;
+  std::vector<int> sz(tiles, smax);
+  if (!uniform && smax < ds::CL) {
+    int left = grid - tiles * smax;
+    for (int t = 0; t < tiles && left >= smax; ++t) {
+      sz[t] = 2 * smax;
+      left -= smax;
+    }
+  }
+  for (int i = 0; i < grid; ++i) out[i] = ds::Work{-1, 0, 0, 0, 0, {0, 0, 0}};
+  const int ncl = grid / ds::CL;
+  std::vector<int> used(ncl, 0);
+  std::vector<int> order(tiles);
+  for (int t = 0; t < tiles; ++t) order[t] = t;
+  std::stable_sort(order.begin(), order.end(), [&](int x, int y) { return sz[x] > sz[y]; });
+  for (int t : order) {
+    const int g = sz[t], kbpc = (nkb + g - 1) / g;
+    int c = 0;
+    while (c < ncl && used[c] + g > ds::CL) ++c;
+    if (c == ncl) return false;
+    const int g0 = used[c];
+    used[c] += g;
+    for (int j = 0; j < g; ++j) {
+      const int kb0 = j * kbpc, nk = std::min(nkb, kb0 + kbpc) - kb0;
+      if (nk <= 0) return false;
+      out[c * ds::CL + g0 + j] = ds::Work{(int16_t)t, (int16_t)g, (int16_t)g0, (int16_t)kb0,
+                                          (int16_t)nk, {0, 0, 0}};
+    }
+  }
+  if (s_out) *s_out = uniform ? smax : 0;
+  return true;
+}
+
+// Decides at context creation whether denoise steps run as one persistent launch, and builds its
+// plans. Requirements: fp16 weights (not quantised), the tensor-core attention with head_dim 256,
+// an action expert of width 1024 (8 tiles × 8-rank splits = the 64 row Σx² partial slots),
+// S ≤ 64 suffix rows, enough co-resident clusters of 8. PI0_STEP_KERNEL=0 in the environment
+// turns it off (the per-kernel chain then runs, for comparisons).
+int setup_step_kernel(pi0_ctx* ctx) {
+  const pi0_config& g = ctx->cfg;
+  ctx->step_kernel = false;
+  const char* env = std::getenv("PI0_STEP_KERNEL");
+  if (env && env[0] == '0') return ctx->step_why = "disabled by PI0_STEP_KERNEL=0", 0;
+  if (g.dtype != PI0_F16 || ctx->qb || !ctx->attn_tc || g.head_dim != 256 || g.num_kv_heads != 1)
+    return ctx->step_why = "needs unquantised fp16 weights and one kv head of dim 256", 0;
+  if (g.ae_width != 1024 || g.action_horizon > ds::NA || g.ae_mlp_dim % 64 ||
+      (g.num_heads * g.head_dim) % 64)
+    return ctx->step_why = "needs an action expert of width 1024 and at most 64 suffix rows", 0;
+  const bool lo = ctx->logits_f32;
+  auto kern = lo ? ds::denoise_step_kernel<true> : ds::denoise_step_kernel<false>;
+  const int smem = std::max(lo ? atc::AtcSmem<256, true>::BYTES : atc::AtcSmem<256, false>::BYTES,
+                            ds::RECV_OFF + ds::RECV_BYTES + 1024);
+  CK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(ds::CL * 16);
+  cfg.blockDim = dim3(ds::NT);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = ds::CL;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  int ncl = 0;
+  CK(cudaOccupancyMaxActiveClusters(&ncl, kern, &cfg));
+  const int S = g.action_horizon, H = g.num_heads, hd = g.head_dim;
+  const int hq = H * hd, W1 = g.ae_width, F1 = g.ae_mlp_dim, P = g.prefix_len;
+  ctx->att_row_tiles = (S * H + 127) / 128;
+  if (ncl < ctx->att_row_tiles || ncl < 2)
+    return ctx->step_why = "too few co-resident clusters of 8", 0;
+  const int grid = ncl * ds::CL;
+  const int N[ds::G_NUM] = {hq + 2 * g.num_kv_heads * hd, W1, 2 * F1, W1};
+  const int K[ds::G_NUM] = {W1, hq, W1, F1};
+  std::vector<ds::Work> plan((size_t)ds::G_NUM * grid);
+  for (int k = 0; k < ds::G_NUM; ++k) {
+    ctx->step_N[k] = N[k];
+    ctx->step_K[k] = K[k];
+    ctx->step_tiles[k] = (N[k] + 127) / 128;
+    ctx->step_nkb[k] = (K[k] + 63) / 64;
+    const bool ssq = k == ds::G_O || k == ds::G_D;  // residual phases: uniform 8-rank groups
+    int su = 0;
+    if (!step_gemm_plan(grid, ctx->step_tiles[k], ctx->step_nkb[k], ssq, &plan[(size_t)k * grid],
+                        &su))
+      return ctx->step_why = "no work plan for a projection", 0;
+    if (ssq && ctx->step_tiles[k] * su != ds::SSQ_PARTS)
+      return ctx->step_why = "residual projections do not give 64 row partials", 0;
+  }
+  ctx->att_ntA = (P + atc::KB - 1) / atc::KB;
+  ctx->att_nt = ctx->att_ntA + (S + atc::KB - 1) / atc::KB;
+  ctx->att_tps = (ctx->att_nt + ds::CL - 1) / ds::CL;
+  ctx->att_splits = (ctx->att_nt + ctx->att_tps - 1) / ctx->att_tps;
+  TRY(dev_alloc(ctx, (void**)&ctx->step_plan, plan.size() * sizeof(ds::Work)));
+  CK(cudaMemcpy(ctx->step_plan, plan.data(), plan.size() * sizeof(ds::Work), cudaMemcpyHostToDevice));
+  std::vector<ds::Layer> layers(g.depth);
+  for (int l = 0; l < g.depth; ++l) {
+    const LayerW& w = ctx->suf[l];
+    layers[l].w[ds::G_QKV] = (const uint8_t*)w.qkv_p;
+    layers[l].w[ds::G_O] = (const uint8_t*)w.o_p;
+    layers[l].w[ds::G_GU] = (const uint8_t*)w.gu_p;
+    layers[l].w[ds::G_D] = (const uint8_t*)w.d_p;
+  }
+  TRY(dev_alloc(ctx, (void**)&ctx->step_layers, layers.size() * sizeof(ds::Layer)));
+  CK(cudaMemcpy(ctx->step_layers, layers.data(), layers.size() * sizeof(ds::Layer),
+                cudaMemcpyHostToDevice));
+  TRY(dev_alloc(ctx, (void**)&ctx->step_bar, sizeof(unsigned long long)));
+  CK(cudaMemset(ctx->step_bar, 0, sizeof(unsigned long long)));
+  ctx->step_grid = grid;
+  ctx->step_kernel = true;
+  ctx->step_why.clear();
+  return 0;
+}
+
+// One denoise step (batch 1) as one persistent launch: x_in the model-dtype x_t (x_is_f32 false)
+// or the fp32 Euler state; out v (euler 0) or the state updated by x += dt·v. The prefix keys'
+// half-scale fp16 copies (and lo parts) must be current (convert_prefix_keys).
+int step_launch(pi0_ctx* ctx, const __half* values, const void* x_in, bool x_is_f32,
+                const __half* mods, const float* scos, const float* ssin, const float* mask,
+                float* out, int euler, float dt, cudaStream_t st) {
+  const pi0_config& g = ctx->cfg;
+  const int S = g.action_horizon, H = g.num_heads, hd = g.head_dim, P = g.prefix_len;
+  const int hq = H * hd, W1 = g.ae_width, F1 = g.ae_mlp_dim, L = g.depth;
+  const bool lo = ctx->logits_f32;
+  CUtensorMap tx, ta, th, tq, tql, tka, tkal, tva, tkb, tkbl, tvb;
+  TRY(make_tmap(ctx, &tx, ctx->xs, S, W1, W1, ds::NA, false));
+  TRY(make_tmap(ctx, &ta, ctx->attn_s, S, hq, hq, ds::NA, false));
+  TRY(make_tmap(ctx, &th, ctx->hs, S, F1, F1, ds::NA, false));
+  TRY(make_tmap(ctx, &tq, ctx->q16s, S * H, hd, hd, 128, false));
+  TRY(make_tmap(ctx, &tql, lo ? ctx->q16s_lo : ctx->q16s, S * H, hd, hd, 128, false));
+  TRY(make_tmap(ctx, &tka, ctx->kpre16, L * P, hd, hd, atc::KB, false));
+  TRY(make_tmap(ctx, &tkal, lo ? ctx->kpre16_lo : ctx->kpre16, L * P, hd, hd, atc::KB, false));
+  TRY(make_tmap(ctx, &tva, values, L * P, hd, hd, atc::KB, false));
+  TRY(make_tmap(ctx, &tkb, ctx->ksuf16, S, hd, hd, atc::KB, false));
+  TRY(make_tmap(ctx, &tkbl, lo ? ctx->ksuf16_lo : ctx->ksuf16, S, hd, hd, atc::KB, false));
+  TRY(make_tmap(ctx, &tvb, ctx->vsuf, S, hd, hd, atc::KB, false));
+  ds::StepArgs a{};
+  a.M = S;
+  a.W1 = W1;
+  a.F1 = F1;
+  a.H = H;
+  a.hd = hd;
+  a.S = S;
+  a.P = P;
+  a.L = L;
+  a.D = g.action_dim;
+  a.layers = ctx->step_layers;
+  a.plan = ctx->step_plan;
+  for (int k = 0; k < ds::G_NUM; ++k) {
+    a.tiles[k] = ctx->step_tiles[k];
+    a.nkb[k] = ctx->step_nkb[k];
+    a.N[k] = ctx->step_N[k];
+    a.K[k] = ctx->step_K[k];
+  }
+  a.mods = mods;
+  a.x = ctx->xs;
+  a.attn = ctx->attn_s;
+  a.h = ctx->hs;
+  a.ssq = ctx->ssq;
+  a.qs = ctx->qs;
+  a.ksuf = ctx->ksuf;
+  a.vsuf = ctx->vsuf;
+  a.q16 = ctx->q16s;
+  a.q16lo = ctx->q16s_lo;
+  a.k16 = ctx->ksuf16;
+  a.k16lo = ctx->ksuf16_lo;
+  a.scos = scos;
+  a.ssin = ssin;
+  a.qscale = (float)std::pow((double)hd, -0.5);
+  a.maskA = mask;
+  a.att_row_tiles = ctx->att_row_tiles;
+  a.att_tps = ctx->att_tps;
+  a.att_splits = ctx->att_splits;
+  a.att_ntA = ctx->att_ntA;
+  a.att_nt = ctx->att_nt;
+  a.kA16 = ctx->kpre16;
+  a.kA16lo = ctx->kpre16_lo;
+  a.vA = values;
+  a.x_in = x_in;
+  a.x_is_f32 = x_is_f32 ? 1 : 0;
+  a.ain_w = ctx->ain_w;
+  a.ain_b = ctx->ain_b;
+  a.aout_w = ctx->aout_w;
+  a.aout_b = ctx->aout_b;
+  a.out = out;
+  a.euler = euler;
+  a.dt = dt;
+  a.eps = g.rms_norm_eps;
+  a.err = ctx->dev_err;
+  a.bar = ctx->step_bar;
+  const int smem = std::max(lo ? atc::AtcSmem<256, true>::BYTES : atc::AtcSmem<256, false>::BYTES,
+                            ds::RECV_OFF + ds::RECV_BYTES + 1024);
+  Prof pr(ctx, F_DEN_STEP, st);
+  ctx->pdl_barrier = true;  // every CTA must be resident together: no overlap with the previous kernel
+  auto kern = lo ? ds::denoise_step_kernel<true> : ds::denoise_step_kernel<false>;
+  TRY(launch(ctx, kern, dim3(ctx->step_grid), dim3(ds::NT), smem, st, dim3(ds::CL, 1, 1), tx, ta,
+             th, tq, tql, tka, tkal, tva, tkb, tkbl, tvb, a));
+  ctx->pdl_barrier = true;
+  return 0;
+}
+
 // ---- prefill ---------------------------------------------------------------------------------
 template <typename T>
 int run_prefill(pi0_ctx* ctx, int B, const T* prefix, const float* mask, float* keys, T* values,
@@ -823,6 +1050,11 @@ int run_suffix(pi0_ctx* ctx, int B, const float* keys, const T* values, const vo
   T* xn = (T*)ctx->xsn;
   T* attn = (T*)ctx->attn_s;
   T* h = (T*)ctx->hs;
+  if constexpr (!Tr<T>::kBf16) {
+    if (ctx->step_kernel && B == 1)  // the whole step as one persistent launch
+      return step_launch(ctx, (const __half*)values, x_in, x_is_f32, (const __half*)mods, scos,
+                         ssin, mask, out, euler, dt, st);
+  }
   {
     Prof pr(ctx, F_DEN_ACT_IN, st);
     const size_t sm = (size_t)D * sizeof(float);
@@ -903,6 +1135,8 @@ int run_step(pi0_ctx* ctx, int B, const float* keys, const T* values, const T* x
              const float* scos, const float* ssin, const float* mask, float* v_out,
              cudaStream_t st) {
   if (ctx->attn_tc) TRY(convert_prefix_keys(ctx, B, keys, st));
+  if (ctx->step_kernel && B == 1)  // a launch cut short can leave arrivals behind: start clean
+    CK(cudaMemsetAsync(ctx->step_bar, 0, sizeof(unsigned long long), st));
   TRY(time_and_mods<T>(ctx, te, 1, st));
   return run_suffix<T>(ctx, B, keys, values, x_t, false, (const T*)ctx->mods, scos, ssin, mask,
                        v_out, 0, 0.f, st);
@@ -919,6 +1153,8 @@ int run_loop_body(pi0_ctx* ctx, int B, const float* keys, const T* values, const
     CK(cudaMemcpyAsync(x_out, x0, (size_t)B * g.action_horizon * g.action_dim * sizeof(float),
                        cudaMemcpyDeviceToDevice, st));
   if (ctx->attn_tc) TRY(convert_prefix_keys(ctx, B, keys, st));
+  if (ctx->step_kernel && B == 1)  // a launch cut short can leave arrivals behind: start clean
+    CK(cudaMemsetAsync(ctx->step_bar, 0, sizeof(unsigned long long), st));
   TRY(time_and_mods<T>(ctx, tes, N, st));
   const float dt = (float)(-1.0 / N);
   for (int i = 0; i < N; ++i)
@@ -1458,6 +1694,7 @@ int pi0_create(const pi0_config* cfg, int device, pi0_ctx** out) {
   CK(cudaStreamCreateWithFlags(&ctx->cap_stream, cudaStreamNonBlocking));
   TRY(alloc_all(ctx));
   TRY(is_bf16(ctx) ? setup_attrs<__nv_bfloat16>(ctx) : setup_attrs<__half>(ctx));
+  TRY(setup_step_kernel(ctx));
   return 0;
 }
 

@@ -121,16 +121,13 @@ __global__ void action_in_kernel(const void* __restrict__ xin, int rows, int D,
 // h = round(norm(x; mod)) with the final norm's modulation (scale, shift); v = float(round(
 // round(h·Wᵀ) + b)); euler = 0: v_out = v; euler = 1: x = x + dt·v (fp32, no fused
 // multiply-add, as numpy and the reference's separate multiply and add). One warp per (row, d).
+// One warp: output d of activation row r (the body of action_out_kernel).
 template <typename T>
-__global__ void action_out_kernel(const T* __restrict__ h, int rows, int Wd,
-                                  const T* __restrict__ mod, float eps,
-                                  const T* __restrict__ W, const T* __restrict__ b, int D,
-                                  float* __restrict__ out, int euler, float dt) {
-  pdl_wait();
-  pdl_trigger();
-  int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-  if (warp >= rows * D) return;
-  int r = warp / D, d = warp - r * D;
+__device__ __forceinline__ void action_out_warp(const T* __restrict__ h, int r, int d, int Wd,
+                                                const T* __restrict__ mod, float eps,
+                                                const T* __restrict__ W, const T* __restrict__ b,
+                                                int D, float* __restrict__ out, int euler,
+                                                float dt, int lane) {
   const uint4* hr = reinterpret_cast<const uint4*>(h + (size_t)r * Wd);
   const uint4* wr = reinterpret_cast<const uint4*>(W + (size_t)d * Wd);
   const int nch = Wd / 8;
@@ -138,7 +135,7 @@ __global__ void action_out_kernel(const T* __restrict__ h, int rows, int Wd,
 #pragma unroll
   for (int c = 0; c < RMS_CHUNKS; ++c)
     if (c * 32 + lane < nch) {
-      hv[c] = __ldg(hr + c * 32 + lane);
+      hv[c] = hr[c * 32 + lane];
       wv[c] = __ldg(wr + c * 32 + lane);
     }
   float ss = 0.f;
@@ -159,8 +156,8 @@ __global__ void action_out_kernel(const T* __restrict__ h, int rows, int Wd,
   for (int c = 0; c < RMS_CHUNKS; ++c)
     if (c * 32 + lane < nch) {
       const int ch = c * 32 + lane;
-      const uint4 sc = __ldg(reinterpret_cast<const uint4*>(mod) + ch);
-      const uint4 sh = __ldg(reinterpret_cast<const uint4*>(mod + Wd) + ch);
+      const uint4 sc = reinterpret_cast<const uint4*>(mod)[ch];
+      const uint4 sh = reinterpret_cast<const uint4*>(mod + Wd)[ch];
       const T* a = reinterpret_cast<const T*>(&hv[c]);
       const T* es = reinterpret_cast<const T*>(&sc);
       const T* eh = reinterpret_cast<const T*>(&sh);
@@ -179,6 +176,19 @@ __global__ void action_out_kernel(const T* __restrict__ h, int rows, int Wd,
     if (euler) *o = __fadd_rn(*o, __fmul_rn(dt, v));
     else *o = v;
   }
+}
+
+template <typename T>
+__global__ void action_out_kernel(const T* __restrict__ h, int rows, int Wd,
+                                  const T* __restrict__ mod, float eps,
+                                  const T* __restrict__ W, const T* __restrict__ b, int D,
+                                  float* __restrict__ out, int euler, float dt) {
+  pdl_wait();
+  pdl_trigger();
+  int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= rows * D) return;
+  int r = warp / D, d = warp - r * D;
+  action_out_warp<T>(h, r, d, Wd, mod, eps, W, b, D, out, euler, dt, lane);
 }
 
 // ---- weight repack: dst row i = src row idx[i] (rows of K elements of 16-bit type) -------

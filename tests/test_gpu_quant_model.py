@@ -96,9 +96,17 @@ def _fused_vs_bind_time(cfg, q, qarrays, deq_arrays, batch):
     outputs of prefill, denoise_step_kv and denoise_loop_kv."""
     from mlc_vla.runtime import Pi0Runtime
 
+    import os
+
     rq = Pi0Runtime(cfg, device=0, quant=q, max_batch=batch)
     rq.bind(rq.to_params(qarrays))
-    rf = Pi0Runtime(cfg, device=0, max_batch=batch)
+    # the same kernels as the quantised context: the per-kernel chain (quantised weights do not
+    # take the persistent step), so the two agree bit for bit
+    os.environ["PI0_STEP_KERNEL"] = "0"
+    try:
+        rf = Pi0Runtime(cfg, device=0, max_batch=batch)
+    finally:
+        del os.environ["PI0_STEP_KERNEL"]
     rf.bind(rf.to_params(deq_arrays))
     inp = recipes.inputs(cfg, seed=1, batch=batch)
     pm, sc, ss, te = _suffix_inputs(cfg, batch)
