@@ -794,15 +794,16 @@ bool step_gemm_plan(int grid, int tiles, int nkb, bool uniform, ds::Work* out, i
 }
 
 // Decides at context creation whether denoise steps run as one persistent launch, and builds its
-// plans. Requirements: fp16 weights (not quantised), the tensor-core attention with head_dim 256,
-// an action expert of width 1024 (8 tiles × 8-rank splits = the 64 row Σx² partial slots),
-// S ≤ 64 suffix rows, enough co-resident clusters of 8. PI0_STEP_KERNEL=0 in the environment
-// turns it off (the per-kernel chain then runs, for comparisons).
+// plans. Opt-in: PI0_STEP_KERNEL=1 in the environment (measured slower than the per-kernel chain
+// on a B200: 1.9 against 1.3 ms per π0.5 step, so the chain is the default). Requirements: fp16
+// weights (not quantised), the tensor-core attention with head_dim 256, an action expert of width
+// 1024 (8 tiles × 8-rank splits = the 64 row Σx² partial slots), S ≤ 64 suffix rows, enough
+// co-resident clusters of 8.
 int setup_step_kernel(pi0_ctx* ctx) {
   const pi0_config& g = ctx->cfg;
   ctx->step_kernel = false;
   const char* env = std::getenv("PI0_STEP_KERNEL");
-  if (env && env[0] == '0') return ctx->step_why = "disabled by PI0_STEP_KERNEL=0", 0;
+  if (!env || env[0] != '1') return ctx->step_why = "not enabled (PI0_STEP_KERNEL=1)", 0;
   if (g.dtype != PI0_F16 || ctx->qb || !ctx->attn_tc || g.head_dim != 256 || g.num_kv_heads != 1)
     return ctx->step_why = "needs unquantised fp16 weights and one kv head of dim 256", 0;
   if (g.ae_width != 1024 || g.action_horizon > ds::NA || g.ae_mlp_dim % 64 ||

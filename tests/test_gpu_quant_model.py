@@ -100,13 +100,9 @@ def _fused_vs_bind_time(cfg, q, qarrays, deq_arrays, batch):
 
     rq = Pi0Runtime(cfg, device=0, quant=q, max_batch=batch)
     rq.bind(rq.to_params(qarrays))
-    # the same kernels as the quantised context: the per-kernel chain (quantised weights do not
-    # take the persistent step), so the two agree bit for bit
-    os.environ["PI0_STEP_KERNEL"] = "0"
-    try:
-        rf = Pi0Runtime(cfg, device=0, max_batch=batch)
-    finally:
-        del os.environ["PI0_STEP_KERNEL"]
+    # the same kernels as the quantised context (the per-kernel chain), so the two agree bit for bit
+    os.environ.pop("PI0_STEP_KERNEL", None)
+    rf = Pi0Runtime(cfg, device=0, max_batch=batch)
     rf.bind(rf.to_params(deq_arrays))
     inp = recipes.inputs(cfg, seed=1, batch=batch)
     pm, sc, ss, te = _suffix_inputs(cfg, batch)

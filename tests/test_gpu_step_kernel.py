@@ -1,5 +1,5 @@
-"""The persistent denoise step (one launch per step, denoise_step.cuh) against the oracle and
-against the per-kernel chain it replaces (the same library with PI0_STEP_KERNEL=0).
+"""The persistent denoise step (one launch per step, denoise_step.cuh; opt-in with
+PI0_STEP_KERNEL=1) against the oracle and against the per-kernel chain, the default path.
 
 Runs at every π0.5 width with two layers (FULL2), batch 1, both attention-logits settings:
 ``denoise_step_kv`` and the 10-step ``denoise_loop_kv`` (reference pi0_model.py:142-194) within
@@ -41,7 +41,11 @@ def _launches(rt):
 @pytest.mark.parametrize("logits", ["float32", "float16"])
 def test_step_kernel_matches_oracle_and_chain(logits):
     cfg = config(recipes.FULL2, attn_logits_dtype=logits)
-    m = Model(cfg)
+    os.environ["PI0_STEP_KERNEL"] = "1"
+    try:
+        m = Model(cfg)
+    finally:
+        del os.environ["PI0_STEP_KERNEL"]
     inp = m.inputs(seed=3)
     nv = 900
     pm = O.prefix_mask(cfg.prefix_len, nv)
@@ -70,11 +74,7 @@ def test_step_kernel_matches_oracle_and_chain(logits):
     # the per-kernel chain on the same weights and inputs
     from mlc_vla.runtime import Pi0Runtime
 
-    os.environ["PI0_STEP_KERNEL"] = "0"
-    try:
-        rt2 = Pi0Runtime(cfg, device=0)
-    finally:
-        del os.environ["PI0_STEP_KERNEL"]
+    rt2 = Pi0Runtime(cfg, device=0)
     rt2.bind(m.params)
     n0 = _launches(rt2)
     vs2 = _np(rt2.denoise_step_kv(k, v, inp["x_t"], inp["time_emb"], sc, ss, pm))
