@@ -106,10 +106,13 @@ NCU_TRAFFIC = {
     "denoise.qkv_rope_gemm": 5465344,
     "denoise.o_gemm": 4541440,
     "denoise.down_gemm": 8940544,
-    "denoise.attention": 1315584,
+    "denoise.attention": 2054144,  # fp32 logits (K hi + lo read); NCU_TRAFFIC_F16 with fp16 logits
     "prefill.gate_up_geglu_gemm": 138220032 + 17278720,
     "prefill.attention": 5023232,
 }
+
+
+NCU_TRAFFIC_F16 = {"denoise.attention": 1315584}
 
 
 # ------------------------------------------------------------------------------------------
@@ -470,7 +473,8 @@ def run_b200(args):
         families[k] = ent
     roofline = {"bound": bound, "kernel": dom, "achieved": round(achieved, 2), "peak": peak,
                 "unit": runit, "frac": round(achieved / peak, 4),
-                "traffic": NCU_TRAFFIC.get(dom), "traffic_unit": "bytes per launch (ncu)",
+                "traffic": (NCU_TRAFFIC_F16.get(dom) if args.attn_logits == "float16" else None)
+                or NCU_TRAFFIC.get(dom), "traffic_unit": "bytes per launch (ncu)",
                 "peak_source": f"{pk_kind} ({'bf16_tflops_sustained' if bound == 'tensor' else 'hbm_gbs'})",
                 "work_per_launch": work / max(1, fam[dom][0]), "families": families}
 
