@@ -142,6 +142,44 @@ def backbone_named_params(config: Pi0Config, dtype: Optional[str] = None,
     return out
 
 
+def vision_named_params(config: Pi0Config, dtype: Optional[str] = None) -> List[Tuple[str, ParamSpec]]:
+    """``[(name, ParamSpec)]`` of the vision stage (``Pi0Model(include={"vision"})``,
+    ``pi0_model.py:76-77``) in the reference's creation order, ``siglip.py:92-102`` with
+    ``SiglipEncoderLayer`` at ``:78-83``, ``SiglipAttention`` at ``:51-56`` and ``SiglipMLP`` at
+    ``:40-42``: ``vision.patch_embedding.{weight,bias}`` ([hidden, p·p·c], the flattened-patch
+    Linear), ``vision.position_embedding`` [num_patches, hidden], per layer
+    ``self_attn.{q,k,v,out}_proj.{weight,bias}``, ``mlp.fc1``, ``mlp.fc2``, ``layer_norm1``,
+    ``layer_norm2`` (``.weight``, ``.bias``), then ``post_layernorm`` and
+    ``multi_modal_projector`` ([projection_dim, hidden]). Every entry in the model dtype."""
+    dt = dtype or config.dtype
+    s = config.siglip
+    h, f = s.hidden_size, s.intermediate_size
+    pdim = s.patch_size * s.patch_size * s.num_channels
+    out: List[Tuple[str, ParamSpec]] = []
+
+    def lin(name, o, i):
+        out.append((name + ".weight", ParamSpec((o, i), dt)))
+        out.append((name + ".bias", ParamSpec((o,), dt)))
+
+    def norm(name, d):
+        out.append((name + ".weight", ParamSpec((d,), dt)))
+        out.append((name + ".bias", ParamSpec((d,), dt)))
+
+    lin("vision.patch_embedding", h, pdim)
+    out.append(("vision.position_embedding", ParamSpec((s.num_patches, h), dt)))
+    for i in range(s.num_hidden_layers):
+        p = f"vision.layers.{i}."
+        for proj in ("q_proj", "k_proj", "v_proj", "out_proj"):
+            lin(p + "self_attn." + proj, h, h)
+        lin(p + "mlp.fc1", f, h)
+        lin(p + "mlp.fc2", h, f)
+        norm(p + "layer_norm1", h)
+        norm(p + "layer_norm2", h)
+    norm("vision.post_layernorm", h)
+    lin("vision.multi_modal_projector", s.projection_dim, h)
+    return out
+
+
 def function_specs(config: Pi0Config, batch: int = 1) -> Dict[str, List[Tuple[str, Tuple[int, ...], str]]]:
     """Argument names, shapes and dtypes of the exported functions.
 
