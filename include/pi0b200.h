@@ -146,6 +146,51 @@ int pi0_embed_language(int dtype, const void* table, int64_t vocab, int width,
                        const int32_t* input_ids, int n_tokens, void* out, int* err,
                        pi0_stream_t stream);
 
+/* ---- the vision stage: vm["embed_image"] ---------------------------------------------------
+ * The reference compiles each stage as its own engine with its own packed parameters
+ * (python/mlc_vla/model/pi0/pi0_model.py:43-58 include_for, :76-77) and calls
+ *   vm["embed_image"](image, params) -> image tokens
+ * (pi0_model.py:97-99, spec :212-215: image [1, 224, 224, 3] model dtype, channels last). These
+ * calls replace that engine: a vision context holds the SigLIP So400m/14 tower and the PaliGemma
+ * projector (siglip.py:20-120). Layouts: image [n, S, S, C] model dtype (S = image_size, C =
+ * num_channels), out [n, T, projection_dim] model dtype, T = (S / patch_size)². */
+typedef struct pi0_vision_ctx pi0_vision_ctx;
+
+/* SiglipConfig (python/mlc_vla/model/pi0/pi0_config.py:60-81) plus the model dtype and the
+ * workspace size. */
+typedef struct pi0_vision_config {
+  int32_t image_size, patch_size, num_channels;   /* 224, 14, 3 */
+  int32_t hidden_size, intermediate_size;         /* 1152, 4304 */
+  int32_t num_hidden_layers, num_attention_heads; /* 27, 16 */
+  int32_t projection_dim;                         /* 2048 (the prefix expert's width) */
+  int32_t dtype;                                  /* pi0_dtype: PI0_F16 or PI0_BF16 */
+  int32_t max_images;                             /* workspace sizing; calls use n ≤ this */
+  float layer_norm_eps;                           /* 1e-6 */
+} pi0_vision_config;
+
+/* Replaces compiling and loading the vision engine (compile.py:99-133 with functions
+ * ["embed_image"]). */
+int pi0_vision_create(const pi0_vision_config* cfg, int device, pi0_vision_ctx** out);
+int pi0_vision_destroy(pi0_vision_ctx* ctx);
+const char* pi0_vision_last_error(const pi0_vision_ctx* ctx);
+/* The vision engine's packed-parameter table (Pi0Model(include={"vision"}).named_params, creation
+ * order of siglip.py:92-102): 3 + 16·layers + 4 entries, every one in the model dtype. */
+int pi0_vision_num_params(const pi0_vision_ctx* ctx);
+int pi0_vision_param_info(const pi0_vision_ctx* ctx, int i, const char** name, int* ndim,
+                          int64_t shape[2], int* dtype);
+int pi0_vision_set_params(pi0_vision_ctx* ctx, const void* const* params, int n,
+                          pi0_stream_t stream);
+/* vm["embed_image"] for n ≤ max_images images at once (the reference runs one image per call);
+ * replayed as one CUDA graph per (n, image, out). image 2-byte and out 4-byte aligned. */
+int pi0_embed_image(pi0_vision_ctx* ctx, int n_images, const void* image, void* out,
+                    pi0_stream_t stream);
+int64_t pi0_vision_launch_count(const pi0_vision_ctx* ctx);
+int pi0_vision_device_error(pi0_vision_ctx* ctx);
+/* pi0_profile_enable / pi0_profile_read for a vision context (families "vision.*"). */
+int pi0_vision_profile_enable(pi0_vision_ctx* ctx, int on);
+int pi0_vision_profile_read(pi0_vision_ctx* ctx, int n_families, int64_t* launches,
+                            double* total_ms);
+
 /* ---- building block and measurement hooks (no counterpart in the reference) --------------- */
 
 /* y[M, N] = x[M, K] · w[N, K]^T in the context's model dtype (fp32 accumulation, one rounding):

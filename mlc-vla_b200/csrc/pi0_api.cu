@@ -169,7 +169,8 @@ namespace {
 enum Fam {
   F_PRE_NORM, F_PRE_QKV, F_PRE_ATTN, F_PRE_O, F_PRE_GU, F_PRE_DOWN,
   F_DEN_TIME_MODS, F_DEN_ACT_IN, F_DEN_NORM, F_DEN_QKV, F_DEN_ATTN, F_DEN_O, F_DEN_GU,
-  F_DEN_DOWN, F_DEN_ACT_OUT, F_DEN_KEYS16, F_DEN_STEP, F_NUM
+  F_DEN_DOWN, F_DEN_ACT_OUT, F_DEN_KEYS16, F_DEN_STEP,
+  F_VIS_PATCH, F_VIS_NORM, F_VIS_QKV, F_VIS_ATTN, F_VIS_O, F_VIS_FC1, F_VIS_FC2, F_VIS_PROJ, F_NUM
 };
 const char* kFamName[F_NUM] = {
   "prefill.rmsnorm", "prefill.qkv_rope_gemm", "prefill.attention", "prefill.o_gemm",
@@ -177,7 +178,9 @@ const char* kFamName[F_NUM] = {
   "denoise.time_mlp_modulation_gemm", "denoise.action_in", "denoise.ada_rmsnorm",
   "denoise.qkv_rope_gemm", "denoise.attention", "denoise.o_gemm", "denoise.gate_up_geglu_gemm",
   "denoise.down_gemm", "denoise.action_out_euler", "denoise.prefix_keys_fp16",
-  "denoise.step_persistent"};
+  "denoise.step_persistent",
+  "vision.patchify_embed_gemm", "vision.layernorm", "vision.qkv_gemm", "vision.attention",
+  "vision.out_gemm", "vision.fc1_gelu_gemm", "vision.fc2_gemm", "vision.projector_gemm"};
 
 int fail(pi0_ctx* c, int code, const std::string& msg) {
   if (c) c->err = msg;
@@ -1656,6 +1659,31 @@ int run_profiled(pi0_ctx* ctx, cudaStream_t stream, F body) {
   return 0;
 }
 
+// Captures `body` (the launches of one call) on the context's capture stream into an executable
+// graph; *nodes = the kernels it launched (a replay adds them to the launch counter).
+template <class F>
+int capture_graph(pi0_ctx* ctx, F body, cudaGraphExec_t* exec, int64_t* nodes) {
+  cudaStream_t cs = ctx->cap_stream;
+  const int64_t before = ctx->launches;
+  CK(cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal));
+  int r = body(cs);
+  cudaGraph_t graph = nullptr;
+  cudaError_t ce = cudaStreamEndCapture(cs, &graph);
+  *nodes = ctx->launches - before;
+  ctx->launches = before;
+  if (r) {
+    if (graph) cudaGraphDestroy(graph);
+    return r;
+  }
+  if (ce != cudaSuccess)
+    return fail(ctx, PI0_ERR_CUDA, std::string("capture: ") + cudaGetErrorString(ce));
+  ce = cudaGraphInstantiate(exec, graph, 0);
+  cudaGraphDestroy(graph);
+  if (ce != cudaSuccess)
+    return fail(ctx, PI0_ERR_CUDA, std::string("instantiate: ") + cudaGetErrorString(ce));
+  return 0;
+}
+
 int check_ready(pi0_ctx* ctx, int batch) {
   if (!ctx) return PI0_ERR_INVALID;
   if (!ctx->have_params) return fail(ctx, PI0_ERR_NO_PARAMS, "pi0_set_params has not been called");
@@ -1827,25 +1855,9 @@ int pi0_denoise_loop_kv(pi0_ctx* ctx, int batch, const float* keys, const void* 
                        nullptr}};
   auto it = ctx->graphs.find(key);
   if (it == ctx->graphs.end()) {
-    cudaStream_t cs = ctx->cap_stream;
-    const int64_t before = ctx->launches;
-    CK(cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal));
-    int r = body(cs);
-    cudaGraph_t graph = nullptr;
-    cudaError_t ce = cudaStreamEndCapture(cs, &graph);
-    const int64_t nodes = ctx->launches - before;
-    ctx->launches = before;
-    if (r) {
-      if (graph) cudaGraphDestroy(graph);
-      return r;
-    }
-    if (ce != cudaSuccess)
-      return fail(ctx, PI0_ERR_CUDA, std::string("capture: ") + cudaGetErrorString(ce));
     cudaGraphExec_t exec = nullptr;
-    ce = cudaGraphInstantiate(&exec, graph, 0);
-    cudaGraphDestroy(graph);
-    if (ce != cudaSuccess)
-      return fail(ctx, PI0_ERR_CUDA, std::string("instantiate: ") + cudaGetErrorString(ce));
+    int64_t nodes = 0;
+    TRY(capture_graph(ctx, body, &exec, &nodes));
     if (ctx->graphs.size() > 64) {
       for (auto& kv : ctx->graphs) cudaGraphExecDestroy(kv.second.first);
       ctx->graphs.clear();
@@ -2107,3 +2119,4 @@ int pi0_linear_noalloc(int dtype, const void* x, int M, int K, const void* w, in
   return linear_noalloc<T>(d, (const T*)x, M, K, (const T*)w, N, (T*)y, stream);
 }
 
+#include "vision_api.cuh"

@@ -39,6 +39,10 @@ EXPORTED = (
     "pi0_profile_read", "pi0_profile_families", "pi0_profile_family_name", "pi0_linear",
     "pi0_device_error", "pi0_div_check", "pi0_linear_noalloc", "pi0_wait_check",
     "pi0_embed_language", "pi0_denoise_step",
+    "pi0_vision_create", "pi0_vision_destroy", "pi0_vision_last_error", "pi0_vision_num_params",
+    "pi0_vision_param_info", "pi0_vision_set_params", "pi0_embed_image",
+    "pi0_vision_launch_count", "pi0_vision_device_error", "pi0_vision_profile_enable",
+    "pi0_vision_profile_read",
 )
 
 
@@ -81,6 +85,19 @@ class Pi0ConfigC(ctypes.Structure):
         ("dtype", ctypes.c_int32), ("quant", ctypes.c_int32), ("max_batch", ctypes.c_int32),
         ("rms_norm_eps", ctypes.c_float), ("rope_theta", ctypes.c_float),
         ("attn_logits", ctypes.c_int32),
+    ]
+
+
+class Pi0VisionConfigC(ctypes.Structure):
+    """Mirror of ``struct pi0_vision_config`` (include/pi0b200.h)."""
+
+    _fields_ = [
+        ("image_size", ctypes.c_int32), ("patch_size", ctypes.c_int32),
+        ("num_channels", ctypes.c_int32), ("hidden_size", ctypes.c_int32),
+        ("intermediate_size", ctypes.c_int32), ("num_hidden_layers", ctypes.c_int32),
+        ("num_attention_heads", ctypes.c_int32), ("projection_dim", ctypes.c_int32),
+        ("dtype", ctypes.c_int32), ("max_images", ctypes.c_int32),
+        ("layer_norm_eps", ctypes.c_float),
     ]
 
 
@@ -130,6 +147,19 @@ def load():
         lib.pi0_denoise_step.argtypes = [vp, i32, vp, vp, vp, vp, vp]
         lib.pi0_wait_check.argtypes = [vp, i32, vp]
         lib.pi0_linear_noalloc.argtypes = [i32, vp, i32, i32, vp, i32, vp, vp]
+        lib.pi0_vision_create.argtypes = [ctypes.POINTER(Pi0VisionConfigC), i32, ctypes.POINTER(vp)]
+        lib.pi0_vision_destroy.argtypes = [vp]
+        lib.pi0_vision_last_error.argtypes = [vp]
+        lib.pi0_vision_last_error.restype = ctypes.c_char_p
+        lib.pi0_vision_num_params.argtypes = [vp]
+        lib.pi0_vision_param_info.argtypes = lib.pi0_param_info.argtypes
+        lib.pi0_vision_set_params.argtypes = [vp, ctypes.POINTER(vp), i32, vp]
+        lib.pi0_embed_image.argtypes = [vp, i32, vp, vp, vp]
+        lib.pi0_vision_launch_count.argtypes = [vp]
+        lib.pi0_vision_launch_count.restype = ctypes.c_int64
+        lib.pi0_vision_device_error.argtypes = [vp]
+        lib.pi0_vision_profile_enable.argtypes = [vp, i32]
+        lib.pi0_vision_profile_read.argtypes = lib.pi0_profile_read.argtypes
         for name in EXPORTED:
             getattr(lib, name).restype = getattr(lib, name).restype or ctypes.c_int
         lib.pi0_last_error.restype = ctypes.c_char_p
@@ -146,8 +176,11 @@ class Pi0Error(RuntimeError):
         self.code = code
 
 
-def check(rc: int, ctx=None, what: str = "") -> None:
+def check(rc: int, ctx=None, what: str = "", vision: bool = False) -> None:
+    """Raise Pi0Error for a nonzero status, with the context's last error text (`vision`: the
+    context is a pi0_vision_ctx)."""
     if rc != PI0_OK:
         lib = load()
-        msg = lib.pi0_last_error(ctx).decode() if ctx else ""
+        err = lib.pi0_vision_last_error if vision else lib.pi0_last_error
+        msg = err(ctx).decode() if ctx else ""
         raise Pi0Error(rc, f"{what}: {msg}" if what else msg)

@@ -53,7 +53,9 @@ def attention(p, pre, x, heads, dt):
     """``siglip.py:50-72`` for x [B, T, hidden] (model dtype)."""
     b, t, hid = x.shape
     hd = hid // heads
-    scale = F32(hd ** -0.5)
+    # ``q * self.scale`` (siglip.py:65): the Relax nn frontend turns a Python scalar operand into
+    # a constant of the tensor's dtype, so the scale itself is rounded to the model dtype
+    scale = rnd(F32(hd ** -0.5), dt)
 
     def proj(name):
         y = linear(x, p[pre + name + ".weight"], p[pre + name + ".bias"], dt)

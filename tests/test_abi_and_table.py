@@ -145,3 +145,63 @@ def test_embed_language_rejects_bad_arguments_before_any_device_work():
     assert lib.pi0_embed_language(_lib.PI0_F16, bad_ptr, 10, 64, ok_ptr, 1, ok_ptr, None, None) == 1
     assert lib.pi0_embed_language(_lib.PI0_F16, ok_ptr, 10, 64, ok_ptr, 1, bad_ptr, None, None) == 1
     assert lib.pi0_embed_language(_lib.PI0_F16, ok_ptr, 10, 64, ok_ptr, 0, ok_ptr, None, None) == 0
+
+
+def _vision_table(cfg):
+    from mlc_vla import _lib
+    from mlc_vla.vision import vision_config_struct
+
+    lib = _lib.load()
+    c = vision_config_struct(cfg, 3)
+    ctx = ctypes.c_void_p()
+    rc = lib.pi0_vision_create(ctypes.byref(c), 0, ctypes.byref(ctx))
+    try:
+        assert rc in (0, _lib.PI0_ERR_CUDA), lib.pi0_vision_last_error(ctx)
+        out = []
+        name, ndim, dt = ctypes.c_char_p(), ctypes.c_int(), ctypes.c_int()
+        shape = (ctypes.c_int64 * 2)()
+        for i in range(lib.pi0_vision_num_params(ctx)):
+            assert lib.pi0_vision_param_info(ctx, i, ctypes.byref(name), ctypes.byref(ndim),
+                                             shape, ctypes.byref(dt)) == 0
+            out.append((name.value.decode(), tuple(shape[j] for j in range(ndim.value)),
+                        _lib.CODE_DTYPE[dt.value]))
+        return out
+    finally:
+        lib.pi0_vision_destroy(ctx)
+
+
+@pytest.mark.parametrize("dtype", ["float16", "bfloat16"])
+def test_vision_table_matches_python_table(dtype):
+    """The vision engine's table (So400m: 439 entries) equals ``vision_named_params``, which is
+    pinned to the reference loader's name map by test_siglip_oracle."""
+    from mlc_vla.model.pi0 import Pi0Config
+    from mlc_vla.model.pi0.pi0_model import vision_named_params
+    from tests.golden import make_siglip_golden as G
+
+    import dataclasses
+
+    for cfg in (Pi0Config(dtype=dtype), G.configs()["mini"]):
+        cfg = dataclasses.replace(cfg, dtype=dtype)
+        mine = [(n, tuple(p.shape), p.dtype) for n, p in vision_named_params(cfg)]
+        assert _vision_table(cfg) == mine
+
+
+def test_invalid_vision_config_rejected_with_message():
+    from mlc_vla import _lib
+
+    lib = _lib.load()
+    base = dict(image_size=224, patch_size=14, num_channels=3, hidden_size=1152,
+                intermediate_size=4304, num_hidden_layers=27, num_attention_heads=16,
+                projection_dim=2048, dtype=_lib.PI0_F16, max_images=3, layer_norm_eps=1e-6)
+    for over, code, text in (({"dtype": _lib.PI0_F32}, _lib.PI0_ERR_UNSUPPORTED, b"float16"),
+                             ({"image_size": 220}, _lib.PI0_ERR_INVALID, b"patch_size"),
+                             ({"num_attention_heads": 6}, _lib.PI0_ERR_UNSUPPORTED, b"head_dim"),
+                             ({"hidden_size": 4096, "num_attention_heads": 32},
+                              _lib.PI0_ERR_UNSUPPORTED, b"2048"),
+                             ({"max_images": 0}, _lib.PI0_ERR_INVALID, b"max_images")):
+        c = _lib.Pi0VisionConfigC(**{**base, **over})
+        ctx = ctypes.c_void_p()
+        rc = lib.pi0_vision_create(ctypes.byref(c), 0, ctypes.byref(ctx))
+        assert rc == code, (over, rc)
+        assert text in lib.pi0_vision_last_error(ctx), (over, lib.pi0_vision_last_error(ctx))
+        lib.pi0_vision_destroy(ctx)
