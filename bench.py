@@ -115,6 +115,38 @@ NCU_TRAFFIC = {
 NCU_TRAFFIC_F16 = {"denoise.attention": 1315584}
 
 
+def roofline_of(fam, wm, traffic):
+    """Roofline of the dominant kernel family of `fam` ({family: (launches, device ms)}) against
+    the measured peaks: achieved = the family's algorithmic work (`wm`) ÷ its device time."""
+    pk, pk_kind = peaks()
+    dom = max(fam, key=lambda k: fam[k][1])
+    work, unit, bound = wm.get(dom, (0, "byte", "hbm"))
+    ms = fam[dom][1]
+    if bound == "tensor":
+        achieved = work / (ms / 1e3) / 1e12
+        peak = pk.get("bf16_tflops_sustained", pk.get("bf16_tflops"))
+        runit = "TFLOP/s"
+    else:
+        achieved = work / (ms / 1e3) / 1e9
+        peak = pk["hbm_gbs"]
+        runit = "GB/s"
+    families = {}
+    for k, (n, tot) in sorted(fam.items(), key=lambda kv: -kv[1][1]):
+        wk = wm.get(k)
+        ent = {"launches": n, "ms": round(tot, 4), "share": round(tot / sum(v[1] for v in fam.values()), 4)}
+        if wk:
+            if wk[2] == "tensor":
+                ent["tflops"] = round(wk[0] / (tot / 1e3) / 1e12, 1)
+            else:
+                ent["gbs"] = round(wk[0] / (tot / 1e3) / 1e9, 1)
+        families[k] = ent
+    return {"bound": bound, "kernel": dom, "achieved": round(achieved, 2), "peak": peak,
+            "unit": runit, "frac": round(achieved / peak, 4), "traffic": traffic.get(dom),
+            "traffic_unit": "bytes per launch (ncu)",
+            "peak_source": f"{pk_kind} ({'bf16_tflops_sustained' if bound == 'tensor' else 'hbm_gbs'})",
+            "work_per_launch": work / max(1, fam[dom][0]), "families": families}
+
+
 # ------------------------------------------------------------------------------------------
 # clocks sampled during the timed region
 # ------------------------------------------------------------------------------------------
@@ -290,9 +322,10 @@ def make_weights(named_params, device, seed=0):
     return out
 
 
-def family_times(rt, fn):
+def family_times(rt, fn, vision=False):
     """{kernel family: (launches, device ms)} of one call of `fn`, replayed from a captured graph
-    in which every launch is bracketed by event-record nodes (the profiled pass)."""
+    in which every launch is bracketed by event-record nodes (the profiled pass). `vision`: `rt`
+    is a VisionRuntime."""
     import ctypes
 
     import torch
@@ -300,14 +333,16 @@ def family_times(rt, fn):
     from mlc_vla import _lib
 
     lib = _lib.load()
-    lib.pi0_profile_enable(rt._ctx, 1)
+    enable = lib.pi0_vision_profile_enable if vision else lib.pi0_profile_enable
+    read = lib.pi0_vision_profile_read if vision else lib.pi0_profile_read
+    enable(rt._ctx, 1)
     fn()
     torch.cuda.synchronize()
     nf = lib.pi0_profile_families()
     launches = (ctypes.c_int64 * nf)()
     total = (ctypes.c_double * nf)()
-    _lib.check(lib.pi0_profile_read(rt._ctx, nf, launches, total), rt._ctx)
-    lib.pi0_profile_enable(rt._ctx, 0)
+    _lib.check(read(rt._ctx, nf, launches, total), rt._ctx, vision=vision)
+    enable(rt._ctx, 0)
     return {lib.pi0_profile_family_name(i).decode(): (int(launches[i]), float(total[i]))
             for i in range(nf) if launches[i]}
 
@@ -447,36 +482,8 @@ def run_b200(args):
         e2e = {"value": e2e_value, "unit": "chunks/s", "ms_per_step": e2e_ms / args.steps,
                "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(B * S * D * 4)}
 
-    # roofline of the dominant kernel family
-    pk, pk_kind = peaks()
-    wm = work_model(cfg, B)
-    dom = max(fam, key=lambda k: fam[k][1])
-    work, unit, bound = wm.get(dom, (0, "byte", "hbm"))
-    ms = fam[dom][1]
-    if bound == "tensor":
-        achieved = work / (ms / 1e3) / 1e12
-        peak = pk.get("bf16_tflops_sustained", pk.get("bf16_tflops"))
-        runit = "TFLOP/s"
-    else:
-        achieved = work / (ms / 1e3) / 1e9
-        peak = pk["hbm_gbs"]
-        runit = "GB/s"
-    families = {}
-    for k, (n, tot) in sorted(fam.items(), key=lambda kv: -kv[1][1]):
-        wk = wm.get(k)
-        ent = {"launches": n, "ms": round(tot, 4), "share": round(tot / sum(v[1] for v in fam.values()), 4)}
-        if wk:
-            if wk[2] == "tensor":
-                ent["tflops"] = round(wk[0] / (tot / 1e3) / 1e12, 1)
-            else:
-                ent["gbs"] = round(wk[0] / (tot / 1e3) / 1e9, 1)
-        families[k] = ent
-    roofline = {"bound": bound, "kernel": dom, "achieved": round(achieved, 2), "peak": peak,
-                "unit": runit, "frac": round(achieved / peak, 4),
-                "traffic": (NCU_TRAFFIC_F16.get(dom) if args.attn_logits == "float16" else None)
-                or NCU_TRAFFIC.get(dom), "traffic_unit": "bytes per launch (ncu)",
-                "peak_source": f"{pk_kind} ({'bf16_tflops_sustained' if bound == 'tensor' else 'hbm_gbs'})",
-                "work_per_launch": work / max(1, fam[dom][0]), "families": families}
+    traffic = dict(NCU_TRAFFIC, **(NCU_TRAFFIC_F16 if args.attn_logits == "float16" else {}))
+    roofline = roofline_of(fam, work_model(cfg, B), traffic)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -584,6 +591,232 @@ def run_part(args):
     return 0
 
 
+# ------------------------------------------------------------------------------------------
+# --workload embed_image: the vision stage (SigLIP So400m/14 + projector), 3 images per step
+# ------------------------------------------------------------------------------------------
+METRIC_VISION = ("pi0.5 embed_image images/s (SigLIP So400m/14 27 layers + projector, "
+                 "224x224x3 -> 256x2048, fp16); one step = one 3-camera observation")
+VISION_IMAGES = 3
+
+
+def vision_work_model(cfg, n):
+    """family -> (work per call of n images, unit, bound): GEMM and attention FLOPs (the patch
+    GEMM at the unpadded K = p·p·C), LayerNorm bytes (read + write once)."""
+    s = cfg.siglip
+    L, W, F, H = s.num_hidden_layers, s.hidden_size, s.intermediate_size, s.num_attention_heads
+    T, hd, pd = s.num_patches, s.head_dim, s.patch_size * s.patch_size * s.num_channels
+    M = n * T
+    return {
+        "vision.patchify_embed_gemm": (2 * M * pd * W, "flop", "tensor"),
+        "vision.qkv_gemm": (L * 2 * M * W * 3 * W, "flop", "tensor"),
+        "vision.attention": (L * 4 * n * H * T * T * hd, "flop", "tensor"),
+        "vision.out_gemm": (L * 2 * M * W * W, "flop", "tensor"),
+        "vision.fc1_gelu_gemm": (L * 2 * M * W * F, "flop", "tensor"),
+        "vision.fc2_gemm": (L * 2 * M * F * W, "flop", "tensor"),
+        "vision.projector_gemm": (2 * M * W * s.projection_dim, "flop", "tensor"),
+        "vision.layernorm": ((2 * L + 1) * 2 * M * W * 2, "byte", "hbm"),
+    }
+
+
+def vision_weights(named_params, device, seed=0):
+    """make_weights draws with 1 added to every LayerNorm weight."""
+    out = make_weights(named_params, device, seed)
+    for t, (name, _) in zip(out, named_params):
+        if name.endswith(("layer_norm1.weight", "layer_norm2.weight", "post_layernorm.weight")):
+            t.add_(1.0)
+    return out
+
+
+class CpuVision:
+    """The numpy SigLIP oracle on one 224×224×3 image per step (27 layers + projector, fp16
+    rounding emulated on fp32 BLAS)."""
+
+    SAMPLE = ("numpy SigLIP oracle (fp32 BLAS, fp16 rounding emulated): one image per step, "
+              "27 layers + post LayerNorm + projector; layers share one weight draw")
+
+    def __init__(self):
+        from mlc_vla.model.pi0 import Pi0Config
+        from mlc_vla.model.pi0.pi0_model import vision_named_params
+        from oracle import pi0_oracle as O
+        from oracle import siglip_oracle as S
+
+        self.S = S
+        self.cores = cpu_threads()
+        self.cfg = Pi0Config(dtype="float16")
+        rng = np.random.default_rng(0)
+        drawn, self.p = {}, {}
+        for name, spec in vision_named_params(self.cfg):
+            # vision.layers.<i>.<rest>: one draw per <rest>, shared by every layer i (each layer
+            # still computes in full; set-up stays short)
+            key = ".".join(name.split(".")[3:]) if name.startswith("vision.layers.") else name
+            if key not in drawn:
+                w = rng.standard_normal(tuple(int(x) for x in spec.shape), dtype=np.float32)
+                w *= np.float32(0.02)
+                if name.endswith(("layer_norm1.weight", "layer_norm2.weight", "post_layernorm.weight")):
+                    w += np.float32(1.0)
+                drawn[key] = O.rnd(w, "float16")
+            self.p[name] = drawn[key]
+        sg = self.cfg.siglip
+        self.image = rng.uniform(-1, 1, (1, sg.image_size, sg.image_size, sg.num_channels)).astype(np.float32)
+
+    def image_ms(self):
+        t0 = time.perf_counter()
+        self.S.embed_image(self.p, self.cfg, self.image)
+        return (time.perf_counter() - t0) * 1e3
+
+
+def run_vision_reference(args):
+    if int(os.environ.get("RANK", "0")) != 0:
+        return 0
+    cpu = CpuVision()
+    for _ in range(min(args.warmup, 1)):
+        cpu.image_ms()
+    t = [cpu.image_ms() for _ in range(args.steps)]
+    ms = float(np.mean(t))
+    value = 1000.0 / ms
+    line = {
+        "metric": METRIC_VISION, "value": value, "unit": "images/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms * VISION_IMAGES,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic", "impl": "reference",
+        "config": {"workload": "embed_image fp16, SigLIP So400m/14 (host CPU, one image per step)",
+                   "global_batch": 1, "seq_len": 256, "parallelism": "cpu"},
+        "cpu_baseline": {"value": value, "unit": "images/s", "cores": cpu.cores, "kind": "port",
+                         "sample": CpuVision.SAMPLE + f"; {args.steps} images timed, "
+                         f"{min(args.warmup, 1)} untimed"},
+        "e2e": {"value": value, "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_vision(args):
+    import torch
+    import torch.distributed as dist
+
+    from mlc_vla.model.pi0 import Pi0Config
+    from mlc_vla.replicas import whole_job_throughput
+    from mlc_vla.vision import VisionRuntime
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    cfg = Pi0Config(dtype="float16")
+    n = VISION_IMAGES * args.batch
+    rt = VisionRuntime(cfg, device=local, max_images=n)
+    params = vision_weights(rt.named_params, dev, seed=0)
+    rt.bind(params)
+    sg = cfg.siglip
+    gen = torch.Generator(device=dev).manual_seed(1000 + rank)
+    images = (torch.rand((n, sg.image_size, sg.image_size, sg.num_channels), generator=gen,
+                         device=dev) * 2 - 1).to(torch.float16)
+    out = torch.empty((n, sg.num_patches, sg.projection_dim), dtype=torch.float16, device=dev)
+
+    def once():
+        rt.embed_image(images, out=out)
+
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(args.warmup):
+        once()
+    torch.cuda.synchronize(dev)
+    fam = family_times(rt, once, vision=True)
+    for _ in range(2):
+        once()
+    torch.cuda.synchronize(dev)
+
+    barrier()
+    torch.cuda.synchronize(dev)
+    n0 = rt.launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        e0.record(stream)
+        for _ in range(args.steps):
+            once()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+    n_launch = rt.launch_count() - n0
+    elapsed = e0.elapsed_time(e1)
+    barrier()
+    value, elapsed_max = whole_job_throughput(elapsed, n * args.steps)
+    ms_step = elapsed_max / args.steps
+
+    # end to end through the public API: pinned host images up, image tokens down
+    e2e = None
+    if not args.no_e2e:
+        host = images.cpu().pin_memory()
+        host_out = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+        dimg = torch.empty_like(images)
+
+        def e2e_once():
+            dimg.copy_(host, non_blocking=True)
+            rt.embed_image(dimg, out=out)
+            host_out.copy_(out, non_blocking=True)
+
+        for _ in range(max(1, args.warmup)):
+            e2e_once()
+        torch.cuda.synchronize(dev)
+        barrier()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record(stream)
+        for _ in range(args.steps):
+            e2e_once()
+        f1.record(stream)
+        torch.cuda.synchronize(dev)
+        e2e_value, e2e_ms = whole_job_throughput(f0.elapsed_time(f1), n * args.steps)
+        e2e = {"value": e2e_value, "unit": "images/s", "ms_per_step": e2e_ms / args.steps,
+               "h2d_bytes_per_step": int(host.numel() * host.element_size()),
+               "d2h_bytes_per_step": int(host_out.numel() * host_out.element_size())}
+
+    roofline = roofline_of(fam, vision_work_model(cfg, n), NCU_TRAFFIC_VISION)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        c = CpuVision()
+        c.image_ms()
+        cms = c.image_ms()
+        cpu = {"value": 1000.0 / cms, "unit": "images/s", "cores": c.cores, "kind": "port",
+               "sample": CpuVision.SAMPLE + "; one image timed after one untimed",
+               "ms_per_image": round(cms, 1)}
+    if rank == 0:
+        line = {
+            "metric": METRIC_VISION, "value": value, "unit": "images/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic (random N(0,0.02) weights, LayerNorm weights 1 + N(0,0.02); "
+                    "U(-1,1) images; seeded)",
+            "config": {"workload": f"embed_image fp16, {n} images of 224x224x3 per call (one CUDA "
+                                   "graph): patchify + 27 SigLIP layers + post LayerNorm + projector",
+                       "model": "SigLIP So400m/14 + PaliGemma projector",
+                       "global_batch": world * n, "seq_len": sg.num_patches,
+                       "parallelism": f"dp{world} (replicas)",
+                       "l2": "inputs larger than L2 (0.83 GB of weights streamed per call)"},
+            "e2e": e2e, "roofline": roofline, "cpu_baseline": cpu, "clocks": clk.summary(),
+            "gpu_launches": int(n_launch),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    rt.close()
+    return 0
+
+
+# DRAM bytes per launch of the vision families from one ncu capture (filled from profiles/)
+NCU_TRAFFIC_VISION = {}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -604,7 +837,12 @@ def main():
                          "default float32, or float16 for its tensor-core option)")
     ap.add_argument("--layers", type=int, default=18, choices=[2, 18],
                     help="with --part: 2 = full widths with two layers, for small profiler captures")
+    ap.add_argument("--workload", default="chunk", choices=["chunk", "embed_image"],
+                    help="chunk: the action-chunk hot path (default); embed_image: the vision "
+                         "stage, 3 images per step")
     args = ap.parse_args()
+    if args.workload == "embed_image":
+        return run_vision_reference(args) if args.impl == "reference" else run_vision(args)
     if args.part != "chunk":
         return run_part(args)
     if args.impl == "reference":

@@ -6,7 +6,7 @@
 //   * one thread issues tcgen05.mma (kind::f16, M=128, N=BN, K=16 per instruction) with the
 //     accumulator in tensor memory; tcgen05.commit releases ring slots and hands finished
 //     accumulators to the epilogue;
-//   * the accumulator is double buffered in TMEM (2·BN columns), so four epilogue warps drain
+//   * the accumulator is double buffered in TMEM (2·BN columns), so eight epilogue warps drain
 //     tile i (tcgen05.ld → registers → functor) while the MMA warp accumulates tile i+1;
 //   * persistent CTAs (one per SM) walk the tiles M-fastest, so the CTAs working at the same
 //     time share W tiles through L2 and every weight byte comes from HBM about once.
@@ -23,6 +23,10 @@ namespace tc {
 
 constexpr int BM = 128;
 constexpr int BK = 64;                       // 64 × 16-bit = one 128-byte swizzle row
+// epilogue warps: two per TMEM lane quarter (a warp may only read its quarter's lanes), taking
+// alternate 32-column chunks of the tile, so a tile drains twice as fast as with one per quarter
+constexpr int EPI_WARPS = 8;
+constexpr int NT = 64 + 32 * EPI_WARPS;      // + the TMA producer warp and the MMA warp
 constexpr unsigned long long kTimeoutNs = 1000000000ull;
 
 enum ErrCode { ERR_NONE = 0, ERR_TIMEOUT_PRODUCER = 1, ERR_TIMEOUT_MMA = 2, ERR_TIMEOUT_EPI = 3 };
@@ -190,7 +194,7 @@ struct Smem {
 // and after a cluster barrier adds the peer's parked half to its own through distributed shared
 // memory (p0 + p1, the same sum on both ranks) before the epilogue.
 template <typename T, int BN, int STAGES, class Epi, int KS = 1>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(NT, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    int M, int N, int K, Epi epi, int* err) {
   using S = Smem<BN, STAGES>;
@@ -219,7 +223,7 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 4);
+      mbar_init(&tempty[a], EPI_WARPS);
     }
     mbar_init(&drain, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -301,7 +305,7 @@ __global__ void __launch_bounds__(192, 1)
       mbar_wait(&drain, 0, err, ERR_TIMEOUT_MMA, false);
     }
   } else if (KS > 1) {  // split-K pair: park the peer's half of the accumulator
-    const int q = warp & 3;
+    const int q = warp & 3, half = (warp - 2) >> 2;
     bool ok = t_first < tiles && nk > 0;
     if (ok && lane == 0) ok = mbar_wait(&tfull[0], 0, err, ERR_TIMEOUT_EPI);
     ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
@@ -312,7 +316,7 @@ __global__ void __launch_bounds__(192, 1)
       float* park = reinterpret_cast<float*>(sbase) + (q * 32 + lane) * XLD;
       const int pc0 = (1 - (int)rank) * H;
 #pragma unroll 1
-      for (int c = 0; c < H; c += 32) {
+      for (int c = half * 32; c < H; c += 64) {
         uint32_t v[32];
         tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + pc0 + c, v);
 #pragma unroll
@@ -322,8 +326,8 @@ __global__ void __launch_bounds__(192, 1)
                           __uint_as_float(v[4 * u + 2]), __uint_as_float(v[4 * u + 3]));
       }
     }
-  } else {  // epilogue warps 2..5: TMEM lane quarter = warp % 4
-    const int q = warp & 3;
+  } else {  // epilogue warps 2..9: TMEM lane quarter = warp % 4, chunk parity = (warp - 2) / 4
+    const int q = warp & 3, half = (warp - 2) >> 2;
     int i = 0;
     for (int t = t_first; t < tiles; t += t_step, ++i) {
       const int acc = i & 1;
@@ -336,15 +340,15 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_after();
       const int row = m0 + q * 32 + lane;
       // one thread per accumulator row; each 32-column chunk goes through the functor's
-      // vectorised chunk32 (operands loaded before results are stored), the next chunk's
-      // operands are requested into L1 while this one is finished
-      if (row < M) epi.prefetch(row, n0);
+      // vectorised chunk32 (operands loaded before results are stored), the warp's next
+      // chunk's operands are requested into L1 while this one is finished
+      if (row < M && half * 32 < BN) epi.prefetch(row, n0 + half * 32);
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
+      for (int c = half * 32; c < BN; c += 64) {
         uint32_t v[32];
         tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + acc * BN + c, v);
         if (row < M) {
-          if (c + 32 < BN && n0 + c + 32 < N) epi.prefetch(row, n0 + c + 32);
+          if (c + 64 < BN && n0 + c + 64 < N) epi.prefetch(row, n0 + c + 64);
           const float* vf = reinterpret_cast<const float*>(v);
           if (!(n0 + c + 32 <= N && epi.chunk32(row, n0 + c, vf))) {
 #pragma unroll
@@ -369,14 +373,14 @@ __global__ void __launch_bounds__(192, 1)
     if (warp >= 2 && epi_ok) {
       tc_fence_after();
       constexpr int H = BN / 2, XLD = H + 4;
-      const int q = warp & 3, t = t_first;
+      const int q = warp & 3, half = (warp - 2) >> 2, t = t_first;
       const int m0 = (t % m_tiles) * BM, n0 = (t / m_tiles) * BN + (int)rank * H;
       const int row = m0 + q * 32 + lane;
       const uint32_t peer = map_rank(
           smem_u32(reinterpret_cast<float*>(sbase) + (q * 32 + lane) * XLD), 1u - rank);
-      if (row < M) epi.prefetch(row, n0);
+      if (row < M) epi.prefetch(row, n0 + half * 32);
 #pragma unroll 1
-      for (int c = 0; c < H; c += 32) {
+      for (int c = half * 32; c < H; c += 64) {
         uint32_t v[32];
         tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (int)rank * H + c, v);
         float4 pv[8];
@@ -391,7 +395,7 @@ __global__ void __launch_bounds__(192, 1)
           vf[4 * u + 3] = __uint_as_float(v[4 * u + 3]) + pv[u].w;
         }
         if (row < M) {
-          if (c + 32 < H && n0 + c + 32 < N) epi.prefetch(row, n0 + c + 32);
+          if (c + 64 < H && n0 + c + 64 < N) epi.prefetch(row, n0 + c + 64);
           if (!(n0 + c + 32 <= N && epi.chunk32(row, n0 + c, vf))) {
 #pragma unroll
             for (int j = 0; j < 16; ++j) {

@@ -401,7 +401,7 @@ int gemm_tc_launch(pi0_ctx* ctx, const T* A, int lda, const T* W, int ldw, int M
   const int tiles = ((M + tc::BM - 1) / tc::BM) * ((N + BN - 1) / BN);
   const int grid = std::min(tiles, ctx->num_sms);
   Prof pr(ctx, fam, st);
-  return launch(ctx, tc::gemm_tc_kernel<T, BN, ST, Epi>, dim3(grid), dim3(192),
+  return launch(ctx, tc::gemm_tc_kernel<T, BN, ST, Epi>, dim3(grid), dim3(tc::NT),
                 tc::Smem<BN, ST>::BYTES, st, dim3(1, 1, 1), ta, tb, M, N, K, epi, ctx->dev_err);
 }
 
@@ -413,19 +413,19 @@ bool use_splitk_pair(int M, int N, int K, int sms) {
   const int tiles = ((M + tc::BM - 1) / tc::BM) * ((N + 255) / 256);
   return K >= 64 * tc::BK && 2 * tiles <= sms && 4 * tiles > sms;
 }
-template <typename T, class Epi>
+template <typename T, class Epi, int BN = 256, int ST = 4>
 int gemm_tc_pair_launch(pi0_ctx* ctx, const T* A, int lda, const T* W, int ldw, int M, int N,
                         int K, const Epi& epi, cudaStream_t st, int fam) {
   CUtensorMap ta, tb;
   const bool bf = Tr<T>::kBf16;
   TRY(make_tmap(ctx, &ta, A, M, K, lda, tc::BM, bf));
-  TRY(make_tmap(ctx, &tb, W, N, K, ldw, 256, bf));
-  const int tiles = ((M + tc::BM - 1) / tc::BM) * ((N + 255) / 256);
+  TRY(make_tmap(ctx, &tb, W, N, K, ldw, BN, bf));
+  const int tiles = ((M + tc::BM - 1) / tc::BM) * ((N + BN - 1) / BN);
   if ((K + tc::BK - 1) / tc::BK < 2)
     return fail(ctx, PI0_ERR_UNSUPPORTED, "split-K pair: K must span at least two k-blocks");
   Prof pr(ctx, fam, st);
-  return launch(ctx, tc::gemm_tc_kernel<T, 256, 4, Epi, 2>, dim3(2 * tiles), dim3(192),
-                tc::Smem<256, 4>::BYTES, st, dim3(2, 1, 1), ta, tb, M, N, K, epi, ctx->dev_err);
+  return launch(ctx, tc::gemm_tc_kernel<T, BN, ST, Epi, 2>, dim3(2 * tiles), dim3(tc::NT),
+                tc::Smem<BN, ST>::BYTES, st, dim3(2, 1, 1), ta, tb, M, N, K, epi, ctx->dev_err);
 }
 
 template <typename T>

@@ -60,8 +60,8 @@ struct pi0_vision_ctx {
   void *post_w = nullptr, *post_b = nullptr, *proj_w = nullptr, *proj_b = nullptr;
   std::vector<VLayer> layers;
   // workspaces for cfg.max_images images
-  void *patches = nullptr, *x = nullptr, *xn = nullptr, *v = nullptr, *ctxo = nullptr, *h = nullptr;
-  float *q = nullptr, *k = nullptr;
+  void *patches = nullptr, *x = nullptr, *xn = nullptr, *ctxo = nullptr, *h = nullptr;
+  void *q = nullptr, *k = nullptr, *v = nullptr;  // model dtype, head-padded
   std::map<VisionKey, std::pair<cudaGraphExec_t, int64_t>> graphs;
 };
 
@@ -173,14 +173,12 @@ int vision_alloc(pi0_vision_ctx* v) {
   TRY(dev_alloc(ctx, &v->patches, M * v->kpad * e));
   TRY(dev_alloc(ctx, &v->x, M * W * e));
   TRY(dev_alloc(ctx, &v->xn, M * W * e));
-  TRY(dev_alloc(ctx, (void**)&v->q, M * H * hdp * 4));
-  TRY(dev_alloc(ctx, (void**)&v->k, M * H * hdp * 4));
-  TRY(dev_alloc(ctx, &v->v, M * H * hdp * e));
+  for (void** p : {&v->q, &v->k, &v->v}) {
+    TRY(dev_alloc(ctx, p, M * H * hdp * e));
+    CK(cudaMemset(*p, 0, M * H * hdp * e));
+  }
   TRY(dev_alloc(ctx, &v->ctxo, M * H * hdp * e));
   TRY(dev_alloc(ctx, &v->h, M * F * e));
-  CK(cudaMemset(v->q, 0, M * H * hdp * 4));
-  CK(cudaMemset(v->k, 0, M * H * hdp * 4));
-  CK(cudaMemset(v->v, 0, M * H * hdp * e));
   TRY(dev_alloc(ctx, (void**)&ctx->dev_err, sizeof(int)));
   CK(cudaMemset(ctx->dev_err, 0, sizeof(int)));
   return 0;
@@ -192,6 +190,26 @@ int attr_tc_all(pi0_ctx* ctx) {
   TRY((attr_tc<T, 256, 4, Epi, 2>(ctx)));
   TRY((attr_tc<T, 160, 5, Epi>(ctx)));
   TRY((attr_tc<T, 128, 6, Epi>(ctx)));
+  TRY((attr_tc<T, 128, 6, Epi, 2>(ctx)));
+  return 0;
+}
+
+// Projection of the vision stage. The row count is small (256 per image), so a GEMM whose
+// 128×128 tiles cover under half of the SMs (the N = hidden projections: 54 tiles for three
+// images) splits K between the two CTAs of a cluster pair; otherwise the automatic tiling.
+template <typename T, class Epi>
+int vision_gemm(pi0_ctx* ctx, const T* A, int lda, const T* W, int ldw, int M, int N, int K,
+                const Epi& epi, cudaStream_t st, int fam) {
+  const int tiles128 = ((M + tc::BM - 1) / tc::BM) * ((N + 127) / 128);
+  if (M > 128 && 2 * tiles128 <= ctx->num_sms && (K + tc::BK - 1) / tc::BK >= 8)
+    return gemm_tc_pair_launch<T, Epi, 128, 6>(ctx, A, lda, W, ldw, M, N, K, epi, st, fam);
+  return gemm<T>(ctx, A, lda, W, ldw, M, N, K, epi, st, fam, M > 128 ? 0 : 1);
+}
+
+template <typename T, int HD>
+int attr_vattn(pi0_ctx* ctx) {
+  CK(cudaFuncSetAttribute(vattn_kernel<T, HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                          VattnSmem<HD>::BYTES));
   return 0;
 }
 
@@ -204,11 +222,11 @@ int vision_attrs(pi0_vision_ctx* v) {
   TRY((attr_tc_all<T, EpiBiasGelu<T>>(ctx)));
   TRY((attr_tc_all<T, EpiStore<T>>(ctx)));
   switch (v->hdp) {
-    case 16: return attr_attn<T, 16>(ctx);
-    case 32: return attr_attn<T, 32>(ctx);
-    case 64: return attr_attn<T, 64>(ctx);
-    case 80: return attr_attn<T, 80>(ctx);
-    case 128: return attr_attn<T, 128>(ctx);
+    case 16: return attr_vattn<T, 16>(ctx);
+    case 32: return attr_vattn<T, 32>(ctx);
+    case 64: return attr_vattn<T, 64>(ctx);
+    case 80: return attr_vattn<T, 80>(ctx);
+    case 128: return attr_vattn<T, 128>(ctx);
   }
   return fail(ctx, PI0_ERR_UNSUPPORTED, "vision head_dim");
 }
@@ -276,21 +294,26 @@ int vision_layernorm(pi0_vision_ctx* v, const T* x, T* out, int rows, const void
                 out, rows, v->cfg.hidden_size, v->cfg.layer_norm_eps, (const T*)w, (const T*)b);
 }
 
+template <typename T, int HD>
+int vattn_launch(pi0_vision_ctx* v, int n, cudaStream_t st) {
+  pi0_ctx* ctx = &v->eng;
+  const int T_len = v->np, H = v->cfg.num_attention_heads;
+  Prof pr(ctx, F_VIS_ATTN, st);
+  return launch(ctx, vattn_kernel<T, HD>, dim3((T_len + VA_BQ - 1) / VA_BQ, 1, n * H), dim3(128),
+                VattnSmem<HD>::BYTES, st, dim3(1, 1, 1), (const T*)v->q, (const T*)v->k,
+                (const T*)v->v, (T*)v->ctxo, T_len, H);
+}
+
 template <typename T>
 int vision_attention(pi0_vision_ctx* v, int n, cudaStream_t st) {
-  const int T_len = v->np, H = v->cfg.num_attention_heads;
-  AttnArgs<T> a{v->q, v->k, (const T*)v->v, nullptr, T_len, nullptr, nullptr, 0, T_len, H, H,
-                0, (T*)v->ctxo, 0, 0};
-  // q and k hold model-dtype values, so their 16-bit operands are the fp32 logits exactly
-  pi0_ctx* ctx = &v->eng;
   switch (v->hdp) {
-    case 16: return attn_launch_hd<T, 16>(ctx, a, n, true, st, F_VIS_ATTN);
-    case 32: return attn_launch_hd<T, 32>(ctx, a, n, true, st, F_VIS_ATTN);
-    case 64: return attn_launch_hd<T, 64>(ctx, a, n, true, st, F_VIS_ATTN);
-    case 80: return attn_launch_hd<T, 80>(ctx, a, n, true, st, F_VIS_ATTN);
-    case 128: return attn_launch_hd<T, 128>(ctx, a, n, true, st, F_VIS_ATTN);
+    case 16: return vattn_launch<T, 16>(v, n, st);
+    case 32: return vattn_launch<T, 32>(v, n, st);
+    case 64: return vattn_launch<T, 64>(v, n, st);
+    case 80: return vattn_launch<T, 80>(v, n, st);
+    case 128: return vattn_launch<T, 128>(v, n, st);
   }
-  return fail(ctx, PI0_ERR_UNSUPPORTED, "vision head_dim");
+  return fail(&v->eng, PI0_ERR_UNSUPPORTED, "vision head_dim");
 }
 
 template <typename T>
@@ -299,7 +322,6 @@ int run_embed_image(pi0_vision_ctx* v, int n, const T* image, T* out, cudaStream
   const pi0_vision_config& c = v->cfg;
   const int W = c.hidden_size, F = c.intermediate_size, Pd = c.projection_dim;
   const int H = c.num_attention_heads, np = v->np, M = n * np, HP = H * v->hdp;
-  const int eng = M > 128 ? 0 : 1;  // tcgen05 tiles (automatic tiling above 128 rows)
   T* x = (T*)v->x;
   T* xn = (T*)v->xn;
   {
@@ -309,30 +331,31 @@ int run_embed_image(pi0_vision_ctx* v, int n, const T* image, T* out, cudaStream
                dim3(1, 1, 1), image, (T*)v->patches, n, c.image_size, c.patch_size,
                c.num_channels, v->kpad));
   }
-  TRY(gemm<T>(ctx, (const T*)v->patches, v->kpad, (const T*)v->patch_w, v->kpad, M, W, v->kpad,
-              EpiBiasPos<T>{x, W, (const T*)v->patch_b, (const T*)v->pos, np}, st, F_VIS_PATCH, eng));
+  TRY(vision_gemm<T>(ctx, (const T*)v->patches, v->kpad, (const T*)v->patch_w, v->kpad, M, W,
+                     v->kpad, EpiBiasPos<T>{x, W, (const T*)v->patch_b, (const T*)v->pos, np}, st,
+                     F_VIS_PATCH));
   // hd^-0.5 as a model-dtype constant (the scalar operand of q * scale takes q's dtype)
   const float s32 = (float)std::pow((double)v->hd, -0.5);
   const float qscale = Tr<T>::kBf16 ? __bfloat162float(__float2bfloat16_rn(s32))
                                     : __half2float(__float2half_rn(s32));
   for (const VLayer& ly : v->layers) {
     TRY(vision_layernorm<T>(v, x, xn, M, ly.ln1_w, ly.ln1_b, st));
-    TRY(gemm<T>(ctx, xn, W, (const T*)ly.qkv_w, W, M, 3 * W, W,
-                EpiVisionQkv<T>{v->q, v->k, (T*)v->v, (const T*)ly.qkv_b, np, H, v->hd, v->hdp,
-                                qscale},
-                st, F_VIS_QKV, eng));
+    TRY(vision_gemm<T>(ctx, xn, W, (const T*)ly.qkv_w, W, M, 3 * W, W,
+                       EpiVisionQkv<T>{(T*)v->q, (T*)v->k, (T*)v->v, (const T*)ly.qkv_b, np, H,
+                                       v->hd, v->hdp, qscale},
+                       st, F_VIS_QKV));
     TRY(vision_attention<T>(v, n, st));
-    TRY(gemm<T>(ctx, (const T*)v->ctxo, HP, (const T*)ly.o_w, HP, M, W, HP,
-                EpiResidBias<T>{x, W, (const T*)ly.o_b}, st, F_VIS_O, eng));
+    TRY(vision_gemm<T>(ctx, (const T*)v->ctxo, HP, (const T*)ly.o_w, HP, M, W, HP,
+                       EpiResidBias<T>{x, W, (const T*)ly.o_b}, st, F_VIS_O));
     TRY(vision_layernorm<T>(v, x, xn, M, ly.ln2_w, ly.ln2_b, st));
-    TRY(gemm<T>(ctx, xn, W, (const T*)ly.fc1_w, W, M, F, W,
-                EpiBiasGelu<T>{(T*)v->h, F, (const T*)ly.fc1_b}, st, F_VIS_FC1, eng));
-    TRY(gemm<T>(ctx, (const T*)v->h, F, (const T*)ly.fc2_w, F, M, W, F,
-                EpiResidBias<T>{x, W, (const T*)ly.fc2_b}, st, F_VIS_FC2, eng));
+    TRY(vision_gemm<T>(ctx, xn, W, (const T*)ly.fc1_w, W, M, F, W,
+                       EpiBiasGelu<T>{(T*)v->h, F, (const T*)ly.fc1_b}, st, F_VIS_FC1));
+    TRY(vision_gemm<T>(ctx, (const T*)v->h, F, (const T*)ly.fc2_w, F, M, W, F,
+                       EpiResidBias<T>{x, W, (const T*)ly.fc2_b}, st, F_VIS_FC2));
   }
   TRY(vision_layernorm<T>(v, x, xn, M, v->post_w, v->post_b, st));
-  return gemm<T>(ctx, xn, W, (const T*)v->proj_w, W, M, Pd, W,
-                 EpiStore<T>{out, Pd, (const T*)v->proj_b}, st, F_VIS_PROJ, eng);
+  return vision_gemm<T>(ctx, xn, W, (const T*)v->proj_w, W, M, Pd, W,
+                        EpiStore<T>{out, Pd, (const T*)v->proj_b}, st, F_VIS_PROJ);
 }
 
 }  // namespace
