@@ -306,6 +306,12 @@ __global__ void __launch_bounds__(NT, 1)
     }
   } else if (KS > 1) {  // split-K pair: park the peer's half of the accumulator
     const int q = warp & 3, half = (warp - 2) >> 2;
+    if (t_first < tiles) {  // operands of the columns this rank finishes, requested early
+      const int prow = (t_first % m_tiles) * BM + q * 32 + lane;
+      const int pn0 = (t_first / m_tiles) * BN + (int)rank * (BN / 2);
+      if (prow < M)
+        for (int c = half * 32; c < BN / 2 && pn0 + c < N; c += 64) epi.prefetch(prow, pn0 + c);
+    }
     bool ok = t_first < tiles && nk > 0;
     if (ok && lane == 0) ok = mbar_wait(&tfull[0], 0, err, ERR_TIMEOUT_EPI);
     ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
@@ -333,6 +339,13 @@ __global__ void __launch_bounds__(NT, 1)
       const int acc = i & 1;
       const uint32_t aph = (i >> 1) & 1;
       const int m0 = (t % m_tiles) * BM, n0 = (t / m_tiles) * BN;
+      // request every global operand of this warp's chunks into L1 while the accumulator is
+      // still being computed (the epilogue warps are otherwise idle then)
+      {
+        const int prow = m0 + q * 32 + lane;
+        if (prow < M)
+          for (int c = half * 32; c < BN && n0 + c < N; c += 64) epi.prefetch(prow, n0 + c);
+      }
       bool ok = true;
       if (lane == 0) ok = mbar_wait(&tfull[acc], aph, err, ERR_TIMEOUT_EPI);
       ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
@@ -340,15 +353,12 @@ __global__ void __launch_bounds__(NT, 1)
       tc_fence_after();
       const int row = m0 + q * 32 + lane;
       // one thread per accumulator row; each 32-column chunk goes through the functor's
-      // vectorised chunk32 (operands loaded before results are stored), the warp's next
-      // chunk's operands are requested into L1 while this one is finished
-      if (row < M && half * 32 < BN) epi.prefetch(row, n0 + half * 32);
+      // vectorised chunk32 (operands loaded before results are stored)
 #pragma unroll 1
       for (int c = half * 32; c < BN; c += 64) {
         uint32_t v[32];
         tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + acc * BN + c, v);
         if (row < M) {
-          if (c + 64 < BN && n0 + c + 64 < N) epi.prefetch(row, n0 + c + 64);
           const float* vf = reinterpret_cast<const float*>(v);
           if (!(n0 + c + 32 <= N && epi.chunk32(row, n0 + c, vf))) {
 #pragma unroll
@@ -378,7 +388,6 @@ __global__ void __launch_bounds__(NT, 1)
       const int row = m0 + q * 32 + lane;
       const uint32_t peer = map_rank(
           smem_u32(reinterpret_cast<float*>(sbase) + (q * 32 + lane) * XLD), 1u - rank);
-      if (row < M) epi.prefetch(row, n0 + half * 32);
 #pragma unroll 1
       for (int c = half * 32; c < H; c += 64) {
         uint32_t v[32];
@@ -395,7 +404,6 @@ __global__ void __launch_bounds__(NT, 1)
           vf[4 * u + 3] = __uint_as_float(v[4 * u + 3]) + pv[u].w;
         }
         if (row < M) {
-          if (c + 64 < H && n0 + c + 64 < N) epi.prefetch(row, n0 + c + 64);
           if (!(n0 + c + 32 <= N && epi.chunk32(row, n0 + c, vf))) {
 #pragma unroll
             for (int j = 0; j < 16; ++j) {

@@ -293,7 +293,10 @@ struct EpiBiasPos {
   const T* bias;
   const T* pos;
   int np;
-  __device__ void prefetch(int, int) const {}
+  __device__ void prefetch(int r, int c) const {
+    pf_l1(bias + c);
+    pf_l1(pos + (size_t)(r % np) * ld + c);
+  }
   __device__ void operator()(int r, int c, float v0, float v1) const {
     const T* pr = pos + (size_t)(r % np) * ld + c;
     const float a = Tr<T>::r(Tr<T>::r(v0) + Tr<T>::f(bias[c]));
@@ -328,7 +331,10 @@ struct EpiResidBias {
   T* x;
   int ld;
   const T* bias;
-  __device__ void prefetch(int r, int c) const { pf_l1(x + (size_t)r * ld + c); }
+  __device__ void prefetch(int r, int c) const {
+    pf_l1(x + (size_t)r * ld + c);
+    pf_l1(bias + c);
+  }
   __device__ void operator()(int r, int c, float v0, float v1) const {
     T* p = x + (size_t)r * ld + c;
     const float a = Tr<T>::r(Tr<T>::r(v0) + Tr<T>::f(bias[c]));
@@ -361,7 +367,7 @@ struct EpiBiasGelu {
   T* h;
   int ld;
   const T* bias;
-  __device__ void prefetch(int, int) const {}
+  __device__ void prefetch(int, int c) const { pf_l1(bias + c); }
   __device__ void operator()(int r, int c, float v0, float v1) const {
     const float a = Tr<T>::r(Tr<T>::r(v0) + Tr<T>::f(bias[c]));
     const float b = Tr<T>::r(Tr<T>::r(v1) + Tr<T>::f(bias[c + 1]));
@@ -397,7 +403,7 @@ struct EpiVisionQkv {
   const T* bias;
   int T_len, H, hd, hdp;
   float qscale;  // hd^-0.5 rounded to the model dtype (the constant takes the tensor's dtype)
-  __device__ void prefetch(int, int) const {}
+  __device__ void prefetch(int, int c) const { pf_l1(bias + c); }
   __device__ T* dst(int which, int img, int t, int head, int d) const {
     if (which == 0) return q + (((size_t)img * T_len + t) * H + head) * hdp + d;
     return (which == 1 ? k : v) + (((size_t)img * H + head) * T_len + t) * hdp + d;

@@ -397,18 +397,25 @@ def dequantize_weight(q_weight: torch.Tensor, q_scale: torch.Tensor, preset, k: 
     return w
 
 
-def embed_language(table: torch.Tensor, input_ids, err: Optional[torch.Tensor] = None) -> torch.Tensor:
+def embed_language(table: torch.Tensor, input_ids, err: Optional[torch.Tensor] = None,
+                   out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """``vm["embed_language"]`` (``pi0_model.py:101-104``): token ids [.., T] -> embeddings
     [.., T, width] = table[id] · sqrt(width) in the table's dtype (fp16 / bf16), on the table's
     device. Raises ValueError for an id outside the table unless `err` (a device int32 tensor)
-    is given, in which case it is set to 1 and the row is zero."""
+    is given, in which case it is set to 1 and the row is zero. `out` (optional): a contiguous
+    tensor of T·width elements to write into, e.g. the language rows of a prefix buffer."""
     lib = _lib.load()
     if table.dim() != 2 or not table.is_cuda:
         raise ValueError("table must be a [vocab, width] CUDA tensor")
     dev = table.device
     ids = torch.as_tensor(np.asarray(input_ids) if not isinstance(input_ids, torch.Tensor)
                           else input_ids).to(device=dev, dtype=torch.int32).contiguous()
-    out = torch.empty(tuple(ids.shape) + (table.shape[1],), dtype=table.dtype, device=dev)
+    if out is None:
+        out = torch.empty(tuple(ids.shape) + (table.shape[1],), dtype=table.dtype, device=dev)
+    elif (out.numel() != ids.numel() * table.shape[1] or out.dtype != table.dtype
+          or out.device != dev or not out.is_contiguous()):
+        raise ValueError("out must be a contiguous tensor of n_tokens x width elements of the "
+                         "table's dtype on its device")
     own = err is None
     flag = torch.zeros(1, dtype=torch.int32, device=dev) if own else err
     dcode = _lib.DTYPE_CODE[str(table.dtype).replace("torch.", "")]
