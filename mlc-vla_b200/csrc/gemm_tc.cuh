@@ -204,7 +204,7 @@ __global__ void __launch_bounds__(NT, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sbase = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                               ~static_cast<uintptr_t>(1023));
-  __shared__ __align__(8) uint64_t full[STAGES], empty[STAGES], tfull[2], tempty[2], drain;
+  __shared__ __align__(8) uint64_t full[STAGES], empty[STAGES], tfull[2], tempty[2], drain, recv;
   __shared__ uint32_t s_tmem;
   bool epi_ok = false;  // KS > 1, epilogue warps: this CTA's accumulator is complete
 
@@ -226,6 +226,7 @@ __global__ void __launch_bounds__(NT, 1)
       mbar_init(&tempty[a], EPI_WARPS);
     }
     mbar_init(&drain, 1);
+    mbar_init(&recv, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
@@ -331,6 +332,7 @@ __global__ void __launch_bounds__(NT, 1)
               make_float4(__uint_as_float(v[4 * u]), __uint_as_float(v[4 * u + 1]),
                           __uint_as_float(v[4 * u + 2]), __uint_as_float(v[4 * u + 3]));
       }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // park -> bulk copy engine
     }
   } else {  // epilogue warps 2..9: TMEM lane quarter = warp % 4, chunk parity = (warp - 2) / 4
     const int q = warp & 3, half = (warp - 2) >> 2;
@@ -376,25 +378,45 @@ __global__ void __launch_bounds__(NT, 1)
   }
 
   if constexpr (KS > 1) {
-    // every rank's half is parked: add the peer's half of this rank's columns and finish them
+    // every rank's half is parked: each rank pushes its parked block into the peer's ring with
+    // bulk shared::cluster copies (completing on the peer's recv barrier), then adds the block
+    // it received (local shared memory) to its own half and finishes those columns
+    constexpr int H = BN / 2, XLD = H + 4;
+    constexpr uint32_t PARK = BM * XLD * 4, PART = PARK / 4;
+    static_assert(2 * PARK <= STAGES * S::STAGE && PART % 16 == 0, "park + receive in the ring");
+    if (threadIdx.x == 64) mbar_expect_tx(&recv, PARK);  // armed before the peer can send
     tc_fence_before();
     __syncthreads();
     cluster_sync();
+    if (threadIdx.x == 64 && epi_ok) {
+      const uint32_t src = smem_u32(sbase), dst = map_rank(smem_u32(sbase) + PARK, 1u - rank);
+      const uint32_t mb = map_rank(smem_u32(&recv), 1u - rank);
+#pragma unroll
+      for (uint32_t part = 0; part < 4; ++part)
+        asm volatile(
+            "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], "
+            "%2, [%3];" ::"r"(dst + part * PART),
+            "r"(src + part * PART), "r"(PART), "r"(mb)
+            : "memory");
+    }
+    bool got = false;
     if (warp >= 2 && epi_ok) {
+      if (lane == 0) got = mbar_wait(&recv, 0, err, ERR_TIMEOUT_EPI);
+      got = __shfl_sync(0xffffffffu, got ? 1 : 0, 0) != 0;
+    }
+    if (got) {
       tc_fence_after();
-      constexpr int H = BN / 2, XLD = H + 4;
       const int q = warp & 3, half = (warp - 2) >> 2, t = t_first;
       const int m0 = (t % m_tiles) * BM, n0 = (t / m_tiles) * BN + (int)rank * H;
       const int row = m0 + q * 32 + lane;
-      const uint32_t peer = map_rank(
-          smem_u32(reinterpret_cast<float*>(sbase) + (q * 32 + lane) * XLD), 1u - rank);
+      const float* rcv = reinterpret_cast<const float*>(sbase + PARK) + (q * 32 + lane) * XLD;
 #pragma unroll 1
       for (int c = half * 32; c < H; c += 64) {
         uint32_t v[32];
         tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (int)rank * H + c, v);
         float4 pv[8];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) pv[u] = ld_cluster4(peer + (uint32_t)(c + 4 * u) * 4u);
+        for (int u = 0; u < 8; ++u) pv[u] = *reinterpret_cast<const float4*>(rcv + c + 4 * u);
         float vf[32];
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
@@ -414,7 +436,8 @@ __global__ void __launch_bounds__(NT, 1)
         }
       }
     }
-    cluster_sync();  // the peer may still be reading this CTA's parked half
+    // the peer has received this CTA's block (or given up) before either CTA exits
+    cluster_sync();
   }
 
   tc_fence_before();
