@@ -23,9 +23,10 @@ namespace tc {
 
 constexpr int BM = 128;
 constexpr int BK = 64;                       // 64 × 16-bit = one 128-byte swizzle row
-// epilogue warps: two per TMEM lane quarter (a warp may only read its quarter's lanes), taking
-// alternate 32-column chunks of the tile, so a tile drains twice as fast as with one per quarter
-constexpr int EPI_WARPS = 8;
+// epilogue warps: EPQ per TMEM lane quarter (a warp may only read its quarter's lanes), taking
+// every EPQ-th 32-column chunk of the tile, so a tile drains EPQ times as fast as with one
+constexpr int EPQ = 2;
+constexpr int EPI_WARPS = 4 * EPQ;
 constexpr int NT = 64 + 32 * EPI_WARPS;      // + the TMA producer warp and the MMA warp
 constexpr unsigned long long kTimeoutNs = 1000000000ull;
 
@@ -306,12 +307,12 @@ __global__ void __launch_bounds__(NT, 1)
       mbar_wait(&drain, 0, err, ERR_TIMEOUT_MMA, false);
     }
   } else if (KS > 1) {  // split-K pair: park the peer's half of the accumulator
-    const int q = warp & 3, half = (warp - 2) >> 2;
+    const int q = warp & 3, sub = (warp - 2) >> 2;
     if (t_first < tiles) {  // operands of the columns this rank finishes, requested early
       const int prow = (t_first % m_tiles) * BM + q * 32 + lane;
       const int pn0 = (t_first / m_tiles) * BN + (int)rank * (BN / 2);
       if (prow < M)
-        for (int c = half * 32; c < BN / 2 && pn0 + c < N; c += 64) epi.prefetch(prow, pn0 + c);
+        for (int c = sub * 32; c < BN / 2 && pn0 + c < N; c += 32 * EPQ) epi.prefetch(prow, pn0 + c);
     }
     bool ok = t_first < tiles && nk > 0;
     if (ok && lane == 0) ok = mbar_wait(&tfull[0], 0, err, ERR_TIMEOUT_EPI);
@@ -323,7 +324,7 @@ __global__ void __launch_bounds__(NT, 1)
       float* park = reinterpret_cast<float*>(sbase) + (q * 32 + lane) * XLD;
       const int pc0 = (1 - (int)rank) * H;
 #pragma unroll 1
-      for (int c = half * 32; c < H; c += 64) {
+      for (int c = sub * 32; c < H; c += 32 * EPQ) {
         uint32_t v[32];
         tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + pc0 + c, v);
 #pragma unroll
@@ -334,8 +335,8 @@ __global__ void __launch_bounds__(NT, 1)
       }
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // park -> bulk copy engine
     }
-  } else {  // epilogue warps 2..9: TMEM lane quarter = warp % 4, chunk parity = (warp - 2) / 4
-    const int q = warp & 3, half = (warp - 2) >> 2;
+  } else {  // epilogue warps: TMEM lane quarter = warp % 4, chunk residue = (warp - 2) / 4
+    const int q = warp & 3, sub = (warp - 2) >> 2;
     int i = 0;
     for (int t = t_first; t < tiles; t += t_step, ++i) {
       const int acc = i & 1;
@@ -346,7 +347,7 @@ __global__ void __launch_bounds__(NT, 1)
       {
         const int prow = m0 + q * 32 + lane;
         if (prow < M)
-          for (int c = half * 32; c < BN && n0 + c < N; c += 64) epi.prefetch(prow, n0 + c);
+          for (int c = sub * 32; c < BN && n0 + c < N; c += 32 * EPQ) epi.prefetch(prow, n0 + c);
       }
       bool ok = true;
       if (lane == 0) ok = mbar_wait(&tfull[acc], aph, err, ERR_TIMEOUT_EPI);
@@ -357,7 +358,7 @@ __global__ void __launch_bounds__(NT, 1)
       // one thread per accumulator row; each 32-column chunk goes through the functor's
       // vectorised chunk32 (operands loaded before results are stored)
 #pragma unroll 1
-      for (int c = half * 32; c < BN; c += 64) {
+      for (int c = sub * 32; c < BN; c += 32 * EPQ) {
         uint32_t v[32];
         tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + acc * BN + c, v);
         if (row < M) {
@@ -406,12 +407,12 @@ __global__ void __launch_bounds__(NT, 1)
     }
     if (got) {
       tc_fence_after();
-      const int q = warp & 3, half = (warp - 2) >> 2, t = t_first;
+      const int q = warp & 3, sub = (warp - 2) >> 2, t = t_first;
       const int m0 = (t % m_tiles) * BM, n0 = (t / m_tiles) * BN + (int)rank * H;
       const int row = m0 + q * 32 + lane;
       const float* rcv = reinterpret_cast<const float*>(sbase + PARK) + (q * 32 + lane) * XLD;
 #pragma unroll 1
-      for (int c = half * 32; c < H; c += 64) {
+      for (int c = sub * 32; c < H; c += 32 * EPQ) {
         uint32_t v[32];
         tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (int)rank * H + c, v);
         float4 pv[8];
