@@ -122,15 +122,16 @@ __global__ void regroup_cols_kernel(uint16_t* __restrict__ dst, int dst_ld,
 // normalised by 1/Σ and rounded once.
 //   q [n, T, H, HD], k / v [n, H, T, HD] (HD = the padded head width, zero pad columns),
 //   out [n, T, H·HD]. grid = (ceil(T / 64), 1, n·H), 128 threads: warp w owns query rows
-//   16w .. 16w+15 of the tile; K/V tiles of 64 keys double buffered with cp.async.
-constexpr int VA_BQ = 64, VA_BK = 64;
+//   16w .. 16w+15 of the tile; K/V tiles of 64 keys in a VA_ST-deep cp.async ring, all of them
+//   requested up front when T ≤ 256 (one load latency per CTA instead of one per tile).
+constexpr int VA_BQ = 64, VA_BK = 64, VA_ST = 4;
 template <int HD>
 struct VattnSmem {
   static constexpr int LD = HD + 8;  // 16-bit row stride: conflict-free ldmatrix rows
   static constexpr int Q_BYTES = VA_BQ * LD * 2;
   static constexpr int KV_BYTES = VA_BK * LD * 2;
   static constexpr int STAGE = 2 * KV_BYTES;
-  static constexpr int BYTES = Q_BYTES + 2 * STAGE;
+  static constexpr int BYTES = Q_BYTES + VA_ST * STAGE;
 };
 
 template <typename T, int HD>
@@ -170,8 +171,12 @@ __global__ void __launch_bounds__(128) vattn_kernel(const T* __restrict__ q,
                ok ? 16 : 0);
   }
   const int ntiles = (T_len + VA_BK - 1) / VA_BK;
-  load_kv(0, 0);
-  cp_async_commit();
+  // VA_ST groups in flight (Q travels with tile 0; empty groups keep the count uniform)
+#pragma unroll
+  for (int t = 0; t < VA_ST; ++t) {
+    if (t < ntiles) load_kv(t, t * VA_BK);
+    cp_async_commit();
+  }
 
   const int gq = lane >> 2, tq = lane & 3;
   float o[HD / 8][4];
@@ -181,10 +186,8 @@ __global__ void __launch_bounds__(128) vattn_kernel(const T* __restrict__ q,
   uint32_t qf[HD / 16][4];
 
   for (int t = 0; t < ntiles; ++t) {
-    const int s = t & 1;
-    if (t + 1 < ntiles) load_kv(s ^ 1, (t + 1) * VA_BK);
-    cp_async_commit();
-    cp_async_wait<1>();
+    const int s = t % VA_ST;
+    cp_async_wait<VA_ST - 1>();  // tile t has landed (VA_ST + t groups committed so far)
     __syncthreads();
     if (t == 0) {
 #pragma unroll
@@ -268,7 +271,9 @@ __global__ void __launch_bounds__(128) vattn_kernel(const T* __restrict__ q,
         mma16816<T>(o[i + 1], pf[kt2], bb1);
       }
     }
-    __syncthreads();  // this stage is refilled by the next iteration's prefetch
+    __syncthreads();  // every warp is done with slot s: refill it with tile t + VA_ST
+    if (t + VA_ST < ntiles) load_kv(s, (t + VA_ST) * VA_BK);
+    cp_async_commit();
   }
   cp_async_wait<0>();
 #pragma unroll
