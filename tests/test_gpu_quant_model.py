@@ -1,5 +1,5 @@
-"""GPU: the model with group-quantised Linear weights (q4f16_1, q4bf16_1, q3f16_1; SURVEY C4,
-``quant.py:117-266``, ``compile_quant.quantize_params`` ``compile_quant.py:71-103``).
+"""GPU: the model with group-quantised Linear weights (q4f16_1, q4bf16_1, q3f16_1; the
+quantised serving configuration, ``quant.py:117-266``, ``compile_quant.quantize_params`` ``compile_quant.py:71-103``).
 
 Every Linear weight is quantised with the reference quantiser's semantics (the oracle's restated
 ``GroupQuantize``), the packed (q_weight, q_scale, bias) table is bound through the C ABI, and
