@@ -99,14 +99,15 @@ def test_embed_image_matches_oracle(kind, n, dtype):
     v.rt.close()
 
 
-def test_embed_image_full_so400m_matches_oracle():
-    """All 27 layers at the reference's shapes (224×224×3 -> 256 tokens × 2048), fp16."""
-    cfg = _config("full", "float16")
+@pytest.mark.parametrize("dtype", ["float16", "bfloat16"])
+def test_embed_image_full_so400m_matches_oracle(dtype):
+    """All 27 layers at the reference's shapes (224×224×3 -> 256 tokens × 2048)."""
+    cfg = _config("full", dtype)
     v = Vision(cfg, max_images=1)
     images = _images(cfg, 1)
     got = v.run(images)
     assert got.shape == (1, 256, 2048)
-    _check(got, v.oracle(images), "float16", "so400m 27 layers fp16")
+    _check(got, v.oracle(images), dtype, f"so400m 27 layers {dtype}")
     v.rt.close()
 
 
