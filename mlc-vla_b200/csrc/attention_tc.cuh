@@ -197,26 +197,38 @@ __device__ __forceinline__ void attn_tile(const CUtensorMap& tmQ, const CUtensor
   };
 
   // LO: ring stage j = (key tile j / NKB, head-dim block j % NKB) into K slot j & 1: that block
-  // of Q_lo, K_hi and K_lo
-  auto issue_lo = [&](int j) {
+  // of Q_lo, K_hi and K_lo. issue_lo_k requests the K parts (arming the stage for all three),
+  // issue_lo_q the Q_lo part.
+  auto issue_lo_k = [&](int j) {
     const int s = j & 1, tile = tbeg + j / NKB, kb = j % NKB;
     const bool inA = tile < a.ntA;
     const int y = inA ? a.ya0 + b * a.LA + tile * KB : b * a.LB + (tile - a.ntA) * KB;
     uint8_t* dst = sK(s);
     mbar_expect_tx(&k_full[s], S::K_BYTES);
-    tma_load_2d(dst, &tmQL, &k_full[s], kb * 64, b * a.rows + row0);
     tma_load_2d(dst + S::QBLK, inA ? &tmKA : &tmKB, &k_full[s], kb * 64, y);
     tma_load_2d(dst + S::QBLK + S::KBLK, inA ? &tmKAL : &tmKBL, &k_full[s], kb * 64, y);
   };
+  auto issue_lo_q = [&](int j) {
+    const int s = j & 1, kb = j % NKB;
+    tma_load_2d(sK(s), &tmQL, &k_full[s], kb * 64, b * a.rows + row0);
+  };
 
-  // tiles of the cached prefix do not depend on the previous kernel (LO: the stages also carry
-  // Q_lo, which does)
-  int issued = 0;  // K and V of tiles [0, issued) requested
-  if (!LO && pdl && tid == 0 && a.a_ready)
-    for (; issued < min(n, 2) && tbeg + issued < a.ntA; ++issued) {
-      issue(issued, false);
-      issue(issued, true);
+  // tiles of the cached prefix do not depend on the previous kernel: request them before its
+  // completion (LO: the K parts of the first two ring stages and V of the first two tiles; the
+  // stages' Q_lo, which does depend on it, follows the wait)
+  int issued = 0;     // V (and, !LO, K) of tiles [0, issued) requested
+  int pre_k = 0;      // LO: K parts of ring stages [0, pre_k) requested
+  if (pdl && tid == 0 && a.a_ready) {
+    if constexpr (LO) {
+      for (; pre_k < min(n * NKB, 2) && tbeg + pre_k / NKB < a.ntA; ++pre_k) issue_lo_k(pre_k);
+      for (; issued < min(n, 2) && tbeg + issued < a.ntA; ++issued) issue(issued, true);
+    } else {
+      for (; issued < min(n, 2) && tbeg + issued < a.ntA; ++issued) {
+        issue(issued, false);
+        issue(issued, true);
+      }
     }
+  }
   if (pdl) {
     pdl_trigger();
     pdl_wait();
@@ -230,19 +242,24 @@ __device__ __forceinline__ void attn_tile(const CUtensorMap& tmQ, const CUtensor
         tma_load_2d(sQ + kb * (128 * 128), &tmQ, &q_full, kb * 64, b * a.rows + row0);
       if constexpr (LO) {
         int jk = 0;  // ring stages [0, jk) requested; V of tiles [0, issued)
+        for (int j = 0; j < pre_k; ++j) issue_lo_q(j);  // complete the early stages
+        jk = pre_k;
         for (int i = 0; i < n; ++i) {
           bool ok = true;
           for (int kb = 0; kb < NKB && ok; ++kb) {
             const int j = i * NKB + kb;
+            if (j < pre_k) continue;
             if (j >= 2 && !mbar_wait(&k_empty[j & 1], ((j >> 1) - 1) & 1, a.err,
                                      ERR_TIMEOUT_PRODUCER)) {
               ok = false;
               break;
             }
-            issue_lo(j);
+            issue_lo_k(j);
+            issue_lo_q(j);
             jk = j + 1;
           }
           if (!ok) break;
+          if (i < issued) continue;  // V requested before the dependency wait
           if (i >= 2 && !mbar_wait(&v_empty[i & 1], ((i >> 1) - 1) & 1, a.err, ERR_TIMEOUT_PRODUCER))
             break;
           issue(i, true);

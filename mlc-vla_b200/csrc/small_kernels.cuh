@@ -298,6 +298,9 @@ __global__ void div_check_kernel(const float* __restrict__ a, const float* __res
 template <typename T>
 __global__ void keys_half_scale_kernel(const float4* __restrict__ k, T* __restrict__ k16,
                                        T* __restrict__ k16lo, size_t n4) {
+  // launched with programmatic dependent launch: the cache may still be being written by the
+  // kernel before (a prefill on the same stream)
+  pdl_wait();
   const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n4) return;
   const float4 v = k[i];
