@@ -93,6 +93,47 @@ def test_loop_equals_host_stepped_loop_bitwise(mini):
     assert np.array_equal(x, xg)
 
 
+def test_prefill_then_step_back_to_back_in_one_graph(mini):
+    """prefill immediately followed by denoise_step_kv with nothing between them on the device
+    (both captured into one CUDA graph, the step's first kernel launched programmatically after
+    the prefill's last, which writes the last layer's K/V): the same bits as the two calls run
+    apart. The caches are refilled with a sentinel before the replay, so a read that ran ahead
+    of the prefill's writes would show."""
+    cfg = mini.cfg
+    rt = mini.rt
+    dev = rt.device
+    inp = mini.inputs(seed=7)
+    pm = torch.from_numpy(O.prefix_mask(cfg.prefix_len)).to(dev)
+    sc, ss = [torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+              for a in O.suffix_rope(cfg, cfg.prefix_len)]
+    prefix = torch.from_numpy(inp["prefix"]).to(dev, torch.float16)
+    x = torch.from_numpy(inp["x_t"]).to(dev, torch.float16)
+    te = torch.from_numpy(inp["time_emb"]).reshape(1, -1).to(dev, torch.float16)
+    vlm = cfg.vlm
+    shape = (vlm.depth, 1, vlm.num_kv_heads, cfg.prefix_len, vlm.head_dim)
+    k1 = torch.empty(shape, device=dev)
+    v1 = torch.empty(shape, device=dev, dtype=torch.float16)
+    o1 = torch.empty((1, cfg.action_horizon, cfg.action_dim), device=dev)
+    rt.prefill(prefix, pm, keys=k1, values=v1)
+    torch.cuda.synchronize()
+    rt.denoise_step_kv(k1, v1, x, te, sc, ss, pm, out=o1)
+    torch.cuda.synchronize()
+    k2, v2, o2 = torch.empty_like(k1), torch.empty_like(v1), torch.empty_like(o1)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        rt.prefill(prefix, pm, keys=k2, values=v2)
+        rt.denoise_step_kv(k2, v2, x, te, sc, ss, pm, out=o2)
+    for _ in range(3):
+        k2.fill_(1e4)
+        v2.fill_(1e4)
+        o2.zero_()
+        g.replay()
+        torch.cuda.synchronize()
+        assert rt.device_error() == 0
+        assert torch.equal(k1, k2) and torch.equal(v1, v2) and torch.equal(o1, o2)
+    del g
+
+
 def test_batch_of_requests_matches_single(mini):
     """Independent requests in one call (own prefix, pad mask, RoPE offset) equal B=1 calls."""
     cfg = mini.cfg
