@@ -1,9 +1,9 @@
 // embed_image (SigLIP So400m/14 + PaliGemma projector; reference python/mlc_vla/model/pi0/
-// siglip.py:92-120, pi0_model.py:97-99) on the GPU: the patchify and LayerNorm kernels and the
-// epilogue functors of its projections. The projections themselves run on the tile GEMM engines
-// (gemm_tc.cuh for ≥ 128 rows) and the attention on attention.cuh (fp32 logits), with the head
-// dimension padded to a multiple of 16 (72 -> 80, zero pad columns) so the attention's shapes
-// are supported; the out-projection weight gets matching zero input columns at bind time.
+// siglip.py:92-120, pi0_model.py:97-99) on the GPU: the patchify, LayerNorm and attention
+// kernels and the epilogue functors of its projections. The projections run on the tcgen05 tile
+// GEMM (gemm_tc.cuh); the attention (vattn_kernel below) works on heads padded to a multiple of
+// 16 (72 -> 80, zero pad columns) so its MMA shapes apply; the out-projection weight gets the
+// matching zero input columns at bind time.
 #pragma once
 
 #include "common.cuh"

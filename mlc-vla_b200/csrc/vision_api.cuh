@@ -7,7 +7,7 @@
 // Per call, for n images of T = (image/patch)² patches (rows M = n·T):
 //   patchify (zero-padded to kpad = round_up(p·p·C, 64) columns)
 //   patch GEMM [M, kpad]·[W, kpad]^T  + bias + position embedding          -> x
-//   per layer: LayerNorm -> q/k/v GEMM (bias; q·scale; head-padded fp32 q, k and model-dtype v)
+//   per layer: LayerNorm -> q/k/v GEMM (bias; q·scale; head-padded model-dtype q, k and v)
 //              -> attention (one CTA per 64 query rows of one image and head) -> out GEMM
 //              over the head-padded context (+ bias, residual) -> LayerNorm -> fc1 GEMM (+ bias,
 //              GELU-tanh) -> fc2 GEMM (+ bias, residual)
