@@ -83,6 +83,11 @@ struct AtcArgs {
   int* err;
   int a_ready;        // segment A was written before the previous kernel
   int ya0;            // row of segment A's first key in its tensor map (layer offset)
+  // > 0: the suffix keys are folded into the last prefix tile, whose first `tail` rows are the
+  // prefix's last keys (LA % 64, a multiple of 8) and whose next LB rows are the suffix keys
+  // (tail + LB ≤ 64); the B tensor maps then have boxes of 64 − tail rows and the tail maps of
+  // `tail` rows. 0: segment B has tiles of its own.
+  int tail;
   uint32_t v_lbo, v_sbo;  // MN-major V descriptor: byte stride between 64-dim blocks / 8-key groups
 };
 
@@ -159,6 +164,8 @@ __device__ __forceinline__ void attn_tile(const CUtensorMap& tmQ, const CUtensor
                                           const CUtensorMap& tmVA, const CUtensorMap& tmKB,
                                           const CUtensorMap& tmVB, const CUtensorMap& tmQL,
                                           const CUtensorMap& tmKAL, const CUtensorMap& tmKBL,
+                                          const CUtensorMap& tmKAT, const CUtensorMap& tmVAT,
+                                          const CUtensorMap& tmKALT,
                                           const AtcArgs& a, int b, int row0, int tbeg, int n,
                                           int nsplit, uint32_t rank, uint8_t* base,
                                           AtcShared& sm, uint32_t tmem, bool pdl) {
@@ -184,16 +191,30 @@ __device__ __forceinline__ void attn_tile(const CUtensorMap& tmQ, const CUtensor
   auto sV = [&](int s) { return base + S::Q_BYTES + s * S::STAGE + S::K_BYTES; };
 
   // one K (is_v = false) or V tile of key tile i into ring slot i & 1
+  // the folded tile (a.tail > 0): prefix rows [0, tail) and suffix rows [tail, 64) of one box
+  // position come from two loads; tail is a multiple of 8, so the second box starts on a
+  // 1024-byte swizzle atom and keeps the 128-byte swizzle pattern of the tile
+  auto folded = [&](int tile) { return a.tail > 0 && tile == a.ntA - 1; };
+  auto load_rows = [&](uint8_t* dst, const CUtensorMap* mA, const CUtensorMap* mAt,
+                       const CUtensorMap* mB, uint64_t* bar, int col, int tile) {
+    if (folded(tile)) {
+      tma_load_2d(dst, mAt, bar, col, a.ya0 + b * a.LA + tile * KB);
+      tma_load_2d(dst + a.tail * 128, mB, bar, col, b * a.LB);
+    } else if (tile < a.ntA) {
+      tma_load_2d(dst, mA, bar, col, a.ya0 + b * a.LA + tile * KB);
+    } else {
+      tma_load_2d(dst, mB, bar, col, b * a.LB + (tile - a.ntA) * KB);
+    }
+  };
   auto issue = [&](int i, bool is_v) {
     const int s = i & 1, tile = tbeg + i;
-    const bool inA = tile < a.ntA;
-    const CUtensorMap* m = inA ? (is_v ? &tmVA : &tmKA) : (is_v ? &tmVB : &tmKB);
-    const int y = inA ? a.ya0 + b * a.LA + tile * KB : b * a.LB + (tile - a.ntA) * KB;
     uint64_t* bar = is_v ? &v_full[s] : &k_full[s];
     uint8_t* dst = is_v ? sV(s) : sK(s);
     mbar_expect_tx(bar, is_v ? S::V_BYTES : S::K_BYTES);
 #pragma unroll
-    for (int kb = 0; kb < NKB; ++kb) tma_load_2d(dst + kb * (KB * 128), m, bar, kb * 64, y);
+    for (int kb = 0; kb < NKB; ++kb)
+      load_rows(dst + kb * (KB * 128), is_v ? &tmVA : &tmKA, is_v ? &tmVAT : &tmKAT,
+                is_v ? &tmVB : &tmKB, bar, kb * 64, tile);
   };
 
   // LO: ring stage j = (key tile j / NKB, head-dim block j % NKB) into K slot j & 1: that block
@@ -201,12 +222,10 @@ __device__ __forceinline__ void attn_tile(const CUtensorMap& tmQ, const CUtensor
   // issue_lo_q the Q_lo part.
   auto issue_lo_k = [&](int j) {
     const int s = j & 1, tile = tbeg + j / NKB, kb = j % NKB;
-    const bool inA = tile < a.ntA;
-    const int y = inA ? a.ya0 + b * a.LA + tile * KB : b * a.LB + (tile - a.ntA) * KB;
     uint8_t* dst = sK(s);
     mbar_expect_tx(&k_full[s], S::K_BYTES);
-    tma_load_2d(dst + S::QBLK, inA ? &tmKA : &tmKB, &k_full[s], kb * 64, y);
-    tma_load_2d(dst + S::QBLK + S::KBLK, inA ? &tmKAL : &tmKBL, &k_full[s], kb * 64, y);
+    load_rows(dst + S::QBLK, &tmKA, &tmKAT, &tmKB, &k_full[s], kb * 64, tile);
+    load_rows(dst + S::QBLK + S::KBLK, &tmKAL, &tmKALT, &tmKBL, &k_full[s], kb * 64, tile);
   };
   auto issue_lo_q = [&](int j) {
     const int s = j & 1, kb = j % NKB;
@@ -219,11 +238,12 @@ __device__ __forceinline__ void attn_tile(const CUtensorMap& tmQ, const CUtensor
   int issued = 0;     // V (and, !LO, K) of tiles [0, issued) requested
   int pre_k = 0;      // LO: K parts of ring stages [0, pre_k) requested
   if (pdl && tid == 0 && a.a_ready) {
+    const int nready = a.tail > 0 ? a.ntA - 1 : a.ntA;  // the folded tile holds suffix keys
     if constexpr (LO) {
-      for (; pre_k < min(n * NKB, 2) && tbeg + pre_k / NKB < a.ntA; ++pre_k) issue_lo_k(pre_k);
-      for (; issued < min(n, 2) && tbeg + issued < a.ntA; ++issued) issue(issued, true);
+      for (; pre_k < min(n * NKB, 2) && tbeg + pre_k / NKB < nready; ++pre_k) issue_lo_k(pre_k);
+      for (; issued < min(n, 2) && tbeg + issued < nready; ++issued) issue(issued, true);
     } else {
-      for (; issued < min(n, 2) && tbeg + issued < a.ntA; ++issued) {
+      for (; issued < min(n, 2) && tbeg + issued < nready; ++issued) {
         issue(issued, false);
         issue(issued, true);
       }
@@ -361,6 +381,13 @@ __device__ __forceinline__ void attn_tile(const CUtensorMap& tmQ, const CUtensor
     const uint32_t tO = tS + 256;
     float m_ref = -1e30f, l = 0.f;
     auto mask_of = [&](int tile) -> float {
+      if (folded(tile)) {
+        if (wt < a.tail) {
+          const int key = tile * KB + wt;
+          return a.maskA ? a.maskA[(size_t)b * a.LA + key] : 0.f;
+        }
+        return wt - a.tail < a.LB ? 0.f : -1e30f;
+      }
       if (tile < a.ntA) {
         const int key = tile * KB + wt;
         return key < a.LA ? (a.maskA ? a.maskA[(size_t)b * a.LA + key] : 0.f) : -1e30f;
@@ -584,7 +611,10 @@ __global__ void __launch_bounds__(NT, 1)
                    const __grid_constant__ CUtensorMap tmVA, const __grid_constant__ CUtensorMap tmKB,
                    const __grid_constant__ CUtensorMap tmVB, const __grid_constant__ CUtensorMap tmQL,
                    const __grid_constant__ CUtensorMap tmKAL,
-                   const __grid_constant__ CUtensorMap tmKBL, AtcArgs a) {
+                   const __grid_constant__ CUtensorMap tmKBL,
+                   const __grid_constant__ CUtensorMap tmKAT,
+                   const __grid_constant__ CUtensorMap tmVAT,
+                   const __grid_constant__ CUtensorMap tmKALT, AtcArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -613,7 +643,8 @@ __global__ void __launch_bounds__(NT, 1)
   const uint32_t tmem = s_tmem;
   const int tbeg = blockIdx.y * a.tps;
   const int n = max(0, min(a.nt, tbeg + a.tps) - tbeg);
-  attn_tile<HD, LO>(tmQ, tmKA, tmVA, tmKB, tmVB, tmQL, tmKAL, tmKBL, a, blockIdx.z,
+  attn_tile<HD, LO>(tmQ, tmKA, tmVA, tmKB, tmVB, tmQL, tmKAL, tmKBL, tmKAT, tmVAT, tmKALT, a,
+                    blockIdx.z,
                     blockIdx.x * 128, tbeg, n, gridDim.y, cluster_rank(), base, sm, tmem, true);
   tc_fence_before();
   __syncthreads();

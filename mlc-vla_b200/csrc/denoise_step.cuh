@@ -480,7 +480,8 @@ __device__ __forceinline__ void attn_phase(const CUtensorMap& tmQ, const CUtenso
                                         const CUtensorMap& tmKAL, const CUtensorMap& tmKBL,
                                         const atc::AtcArgs& aa, int row0, int tbeg, int n,
                                         int nsplit, uint32_t rank, uint8_t* base, Sh& sh) {
-  atc::attn_tile<256, LO>(tmQ, tmKA, tmVA, tmKB, tmVB, tmQL, tmKAL, tmKBL, aa, 0, row0, tbeg,
+  atc::attn_tile<256, LO>(tmQ, tmKA, tmVA, tmKB, tmVB, tmQL, tmKAL, tmKBL, tmKA, tmVA, tmKAL, aa,
+                                0, row0, tbeg,
                                 n, nsplit, rank, base, sh.att, sh.tmem, false);
 }
 

@@ -673,13 +673,20 @@ int attn_tc_launch_hd(pi0_ctx* ctx, int B, const __half* q16, const __half* q16l
                       const __half* kB16, const __half* kB16lo, const __half* vB, int LB,
                       const float* mask, __half* out, int a_ready, cudaStream_t st, int fam) {
   const bool lo = q16lo != nullptr;
-  CUtensorMap tq, tka, tva, tkb, tvb, tql, tkal, tkbl;
+  // Fold the suffix keys into the prefix's last, partial tile when they fit in it (decode: 968
+  // prefix keys leave 8 in the last tile, the 50 suffix keys fill it to 58): one tile fewer, so
+  // every key split can hold a single tile. The tile's rows come from two loads whose boxes are
+  // `tail` and 64 − tail rows high.
+  const int tail = LA % atc::KB;
+  const bool fold = a_ready && LB > 0 && tail > 0 && tail % 8 == 0 && tail + LB <= atc::KB;
+  const int brows = fold ? atc::KB - tail : atc::KB;
+  CUtensorMap tq, tka, tva, tkb, tvb, tql, tkal, tkbl, tkat, tvat, tkalt;
   TRY(make_tmap(ctx, &tq, q16, B * rows, HD, HD, 128, false));
   TRY(make_tmap(ctx, &tka, kA16, B * LA, HD, HD, atc::KB, false));
   TRY(make_tmap(ctx, &tva, vA, B * LA, HD, HD, atc::KB, false));
   if (LB > 0) {
-    TRY(make_tmap(ctx, &tkb, kB16, B * LB, HD, HD, atc::KB, false));
-    TRY(make_tmap(ctx, &tvb, vB, B * LB, HD, HD, atc::KB, false));
+    TRY(make_tmap(ctx, &tkb, kB16, B * LB, HD, HD, brows, false));
+    TRY(make_tmap(ctx, &tvb, vB, B * LB, HD, HD, brows, false));
   } else {
     tkb = tka;
     tvb = tva;
@@ -687,19 +694,30 @@ int attn_tc_launch_hd(pi0_ctx* ctx, int B, const __half* q16, const __half* q16l
   if (lo) {
     TRY(make_tmap(ctx, &tql, q16lo, B * rows, HD, HD, 128, false));
     TRY(make_tmap(ctx, &tkal, kA16lo, B * LA, HD, HD, atc::KB, false));
-    if (LB > 0) TRY(make_tmap(ctx, &tkbl, kB16lo, B * LB, HD, HD, atc::KB, false));
+    if (LB > 0) TRY(make_tmap(ctx, &tkbl, kB16lo, B * LB, HD, HD, brows, false));
     else tkbl = tkal;
   } else {
     tql = tq;
     tkal = tka;
     tkbl = tkb;
   }
+  if (fold) {
+    TRY(make_tmap(ctx, &tkat, kA16, B * LA, HD, HD, tail, false));
+    TRY(make_tmap(ctx, &tvat, vA, B * LA, HD, HD, tail, false));
+    if (lo) TRY(make_tmap(ctx, &tkalt, kA16lo, B * LA, HD, HD, tail, false));
+    else tkalt = tkat;
+  } else {
+    tkat = tka;
+    tvat = tva;
+    tkalt = tkal;
+  }
   atc::AtcArgs a{};
   a.rows = rows;
   a.LA = LA;
   a.LB = LB;
   a.ntA = (LA + atc::KB - 1) / atc::KB;
-  a.nt = a.ntA + (LB + atc::KB - 1) / atc::KB;
+  a.nt = fold ? a.ntA : a.ntA + (LB + atc::KB - 1) / atc::KB;
+  a.tail = fold ? tail : 0;
   const int row_tiles = (rows + 127) / 128;
   int splits = std::max(1, std::min(16, ctx->num_sms / std::max(1, row_tiles * B)));
   splits = std::min(splits, a.nt);
@@ -715,10 +733,10 @@ int attn_tc_launch_hd(pi0_ctx* ctx, int B, const __half* q16, const __half* q16l
   if (lo)
     return launch(ctx, atc::attn_tc_kernel<HD, true>, dim3(row_tiles, splits, B), dim3(atc::NT),
                   atc::AtcSmem<HD, true>::BYTES, st, dim3(1, splits, 1), tq, tka, tva, tkb, tvb,
-                  tql, tkal, tkbl, a);
+                  tql, tkal, tkbl, tkat, tvat, tkalt, a);
   return launch(ctx, atc::attn_tc_kernel<HD, false>, dim3(row_tiles, splits, B), dim3(atc::NT),
                 atc::AtcSmem<HD, false>::BYTES, st, dim3(1, splits, 1), tq, tka, tva, tkb, tvb,
-                tql, tkal, tkbl, a);
+                tql, tkal, tkbl, tkat, tvat, tkalt, a);
 }
 
 // q16lo / kA16lo / kB16lo: the fp16 lo parts for fp32 logits (null: model-dtype logits)
