@@ -42,6 +42,7 @@ __global__ void rmsnorm_kernel(const T* __restrict__ x, T* __restrict__ out, int
     }
   ss = warp_sum(ss);
   const float denom = sqrtf(__fadd_rn(__fdiv_rn(ss, (float)W), eps));
+  const float rden = __frcp_rn(denom);  // x / denom below: div_by_rcp, bit-equal to IEEE division
   const T* m = mod ? mod + (size_t)(row / rows_per_mod) * mod_stride : nullptr;
   uint4* o = reinterpret_cast<uint4*>(out + (size_t)row * W);
 #pragma unroll
@@ -65,7 +66,7 @@ __global__ void rmsnorm_kernel(const T* __restrict__ x, T* __restrict__ out, int
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const int q = 2 * j + h;
-        float n = __fdiv_rn(Tr<T>::f(e[q]), denom);
+        float n = div_by_rcp(Tr<T>::f(e[q]), denom, rden);
         r2[h] = m ? __fadd_rn(__fmul_rn(n, __fadd_rn(1.f, Tr<T>::f(sa[q]))), Tr<T>::f(sb[q]))
                   : __fmul_rn(n, __fadd_rn(1.f, Tr<T>::f(sa[q])));
       }

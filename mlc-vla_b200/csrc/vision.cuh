@@ -73,6 +73,7 @@ __global__ void layernorm_kernel(const T* __restrict__ x, T* __restrict__ out, i
       }
   const float var = __fdiv_rn(warp_sum(q), (float)W);
   const float den = sqrtf(__fadd_rn(var, eps));
+  const float rden = __frcp_rn(den);  // (x − mean) / den below: div_by_rcp, bit-equal to IEEE
   uint4* o = reinterpret_cast<uint4*>(out + (size_t)row * W);
 #pragma unroll
   for (int c = 0; c < LN_CHUNKS; ++c) {
@@ -89,7 +90,7 @@ __global__ void layernorm_kernel(const T* __restrict__ x, T* __restrict__ out, i
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const int k = 2 * j + h;
-        const float n = __fdiv_rn(__fsub_rn(v[c][k], mean), den);
+        const float n = div_by_rcp(__fsub_rn(v[c][k], mean), den, rden);
         y[h] = __fadd_rn(__fmul_rn(n, Tr<T>::f(we[k])), Tr<T>::f(be[k]));
       }
       r[j] = Tr<T>::pack(y[0], y[1]);
