@@ -18,7 +18,8 @@ sampled during the timed region, and the number of library kernels launched.
 
 ``--impl reference`` times the reference's CPU implementation of the path — the numpy oracle
 that restates it (the reference itself needs TVM, absent here) — on all host cores, one whole
-chunk per step, and prints the same line with ``"impl": "reference"``.
+chunk per step (until the steps are done or two minutes of chunks have run), and prints the same
+line with ``"impl": "reference"``.
 """
 
 from __future__ import annotations
@@ -282,6 +283,23 @@ class CpuChunk:
 # ------------------------------------------------------------------------------------------
 # reference arm
 # ------------------------------------------------------------------------------------------
+# the reference arm times whole samples until --steps are done or this much host time has gone,
+# so that `--steps K` with the GPU arm's K still ends within a few minutes
+REFERENCE_BUDGET_S = 120.0
+
+
+def timed_samples(fn, steps):
+    """Times fn() (returns ms) up to `steps` times, stopping early once REFERENCE_BUDGET_S of
+    samples have run (at least one sample)."""
+    t, spent = [], 0.0
+    for _ in range(max(1, steps)):
+        t.append(fn())
+        spent += t[-1] / 1e3
+        if spent >= REFERENCE_BUDGET_S:
+            break
+    return t
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -289,7 +307,7 @@ def run_reference(args):
     cpu = CpuChunk()
     for _ in range(args.warmup):
         cpu.warm()
-    t = [cpu.chunk_ms() for _ in range(args.steps)]
+    t = timed_samples(cpu.chunk_ms, args.steps)
     ms = float(np.mean(t))
     value = 1000.0 / ms
     line = {
@@ -300,8 +318,9 @@ def run_reference(args):
         "config": {"workload": "pi0.5 fp16 bs1: prefill(968) + 10 Euler steps (host CPU)",
                    "global_batch": 1, "seq_len": 968, "parallelism": "cpu"},
         "cpu_baseline": {"value": value, "unit": "chunks/s", "cores": cpu.cores, "kind": "port",
-                         "sample": CpuChunk.SAMPLE + f"; {args.steps} chunks timed, warm-up: "
-                         f"{args.warmup} single denoise steps"},
+                         "sample": CpuChunk.SAMPLE + f"; {len(t)} whole chunks timed (of "
+                         f"{args.steps} steps asked; at most {REFERENCE_BUDGET_S:.0f} s of samples), "
+                         f"warm-up: {args.warmup} single denoise steps"},
         "e2e": {"value": value, "unit": "chunks/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -671,7 +690,7 @@ def run_vision_reference(args):
     cpu = CpuVision()
     for _ in range(min(args.warmup, 1)):
         cpu.image_ms()
-    t = [cpu.image_ms() for _ in range(args.steps)]
+    t = timed_samples(cpu.image_ms, args.steps)
     ms = float(np.mean(t))
     value = 1000.0 / ms
     line = {
@@ -682,7 +701,8 @@ def run_vision_reference(args):
         "config": {"workload": "embed_image fp16, SigLIP So400m/14 (host CPU, one image per step)",
                    "global_batch": 1, "seq_len": 256, "parallelism": "cpu"},
         "cpu_baseline": {"value": value, "unit": "images/s", "cores": cpu.cores, "kind": "port",
-                         "sample": CpuVision.SAMPLE + f"; {args.steps} images timed, "
+                         "sample": CpuVision.SAMPLE + f"; {len(t)} images timed (of "
+                         f"{args.steps} steps asked; at most {REFERENCE_BUDGET_S:.0f} s of samples), "
                          f"{min(args.warmup, 1)} untimed"},
         "e2e": {"value": value, "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
