@@ -197,7 +197,8 @@ int pi0_vision_profile_read(pi0_vision_ctx* ctx, int n_families, int64_t* launch
  * the GEMM engine every projection of the path runs on, exposed for direct tests. engine: 0 =
  * automatic, 1 = tcgen05 tiles (M >= 128), 2 = warp-level mma, 3 = tcgen05 weight-streaming
  * split-K (M <= 128), 4 = tcgen05 128×256 tiles split over K between two CTAs of a cluster
- * (M >= 128, K > 64). */
+ * (M >= 128, K > 64), 5 = tcgen05 256×256 tiles on a CTA pair (cta_group::2). Other engine
+ * numbers: PI0_ERR_INVALID. */
 int pi0_linear(pi0_ctx* ctx, const void* x, int M, int K, const void* w, int N, void* y,
                int engine, pi0_stream_t stream);
 

@@ -132,6 +132,45 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
           smem_u32(bar))
       : "memory");
 }
+// ---- CTA-pair forms (tcgen05 cta_group::2): the even CTA of a cluster pair issues one MMA that
+// reads A (128 rows each) and B (half the columns each) from both CTAs' shared memory at the
+// same offsets and writes each CTA's 128 accumulator rows into that CTA's tensor memory ----
+__device__ __forceinline__ void umma_f16_pair(uint32_t tmem_d, uint64_t a, uint64_t b,
+                                              uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
+}
+// arrive on the barrier at this offset in both CTAs of the pair once the pair's MMAs complete
+__device__ __forceinline__ void umma_commit_pair_both(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 "
+      "[%0], %1;" ::"r"(smem_u32(bar)),
+      "h"((uint16_t)0x3)
+      : "memory");
+}
+__device__ __forceinline__ void umma_commit_pair(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+// TMA load into this CTA's shared memory whose completion is counted on `bar_cluster`, a
+// shared::cluster address that may be the peer CTA's barrier (the pair's loads all complete on
+// the even CTA's barrier, where its MMA issuer waits)
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map,
+                                                 uint32_t bar_cluster, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(bar_cluster), "r"(x), "r"(y)
+      : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster)
+               : "memory");
+}
 __device__ __forceinline__ void tc_fence_before() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
 }
@@ -178,10 +217,10 @@ __device__ __forceinline__ float4 ld_cluster4(uint32_t addr) {
   return v;
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, int CG = 1>
 struct Smem {
   static constexpr int A_BYTES = BM * BK * 2;
-  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int B_BYTES = BN / CG * BK * 2;  // a CTA pair stages half of W each
   static constexpr int STAGE = A_BYTES + B_BYTES;
   static constexpr int BYTES = STAGES * STAGE + 1024;  // + alignment slack
   // double-buffered accumulator, rounded up to the power of two tcgen05.alloc requires
@@ -194,14 +233,26 @@ struct Smem {
 // columns [r·BN/2, (r+1)·BN/2): it parks the other half of its accumulator in its drained ring,
 // and after a cluster barrier adds the peer's parked half to its own through distributed shared
 // memory (p0 + p1, the same sum on both ranks) before the epilogue.
-template <typename T, int BN, int STAGES, class Epi, int KS = 1>
+//
+// CG = 2: one 256 × BN output tile per cluster pair on tcgen05 cta_group::2 (persistent pairs,
+// grid = 2·pairs). Each CTA stages its own 128 rows of A and its own BN/2 rows of W per k-block,
+// so a pair moves (256 + BN)·64 elements for a 256 × BN × 64 product where two single CTAs move
+// 2·(128 + BN)·64: a third less shared-memory ingress per SM at BN = 256. The even CTA issues
+// the MMAs; both CTAs' loads complete on its ring barriers (it arms them for the pair's bytes);
+// its commits arrive on the same barrier in both CTAs (ring slots, finished accumulators); both
+// CTAs' epilogue warps drain their own 128 rows from their own tensor memory and report the
+// drained accumulator to the even CTA.
+template <typename T, int BN, int STAGES, class Epi, int KS = 1, int CG = 1>
 __global__ void __launch_bounds__(NT, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    int M, int N, int K, Epi epi, int* err) {
-  using S = Smem<BN, STAGES>;
+  using S = Smem<BN, STAGES, CG>;
   static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN");
   static_assert(KS == 1 || (KS == 2 && BN % 64 == 0 && 128 * (BN / 2 + 4) * 4 <= STAGES * S::STAGE),
                 "split-K pair: parked half must fit the ring");
+  static_assert(CG == 1 || (CG == 2 && KS == 1 && BN % 32 == 0 && BN >= 64),
+                "CTA-pair tiles: no K split, W half at least 32 rows");
+  constexpr int TM = BM * CG;  // rows of one output tile
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sbase = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                               ~static_cast<uintptr_t>(1023));
@@ -210,12 +261,14 @@ __global__ void __launch_bounds__(NT, 1)
   bool epi_ok = false;  // KS > 1, epilogue warps: this CTA's accumulator is complete
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m_tiles = (M + BM - 1) / BM, n_tiles = (N + BN - 1) / BN;
+  const int m_tiles = (M + TM - 1) / TM, n_tiles = (N + BN - 1) / BN;
   const int tiles = m_tiles * n_tiles;
-  const uint32_t rank = KS > 1 ? cluster_rank() : 0;
+  const uint32_t rank = (KS > 1 || CG > 1) ? cluster_rank() : 0;
+  const bool leader = CG == 1 || rank == 0;      // issues the MMAs (CG = 2: the even CTA)
+  const int mrow = CG > 1 ? (int)rank * BM : 0;  // this CTA's rows inside a pair tile
   const int nk_all = (K + BK - 1) / BK, kper = (nk_all + KS - 1) / KS;
-  const int kb0 = (int)rank * kper, nk = max(0, min(nk_all, kb0 + kper) - kb0);
-  const int t_first = blockIdx.x / KS, t_step = gridDim.x / KS;
+  const int kb0 = KS > 1 ? (int)rank * kper : 0, nk = max(0, min(nk_all, kb0 + kper) - kb0);
+  const int t_first = blockIdx.x / (KS * CG), t_step = gridDim.x / (KS * CG);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -224,7 +277,7 @@ __global__ void __launch_bounds__(NT, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], EPI_WARPS);
+      mbar_init(&tempty[a], EPI_WARPS * CG);
     }
     mbar_init(&drain, 1);
     mbar_init(&recv, 1);
@@ -233,13 +286,23 @@ __global__ void __launch_bounds__(NT, 1)
     tma_prefetch_desc(&tmB);
   }
   if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                     smem_u32(&s_tmem)),
-                 "r"(S::TMEM_COLS));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    if constexpr (CG == 2) {  // the same columns in both CTAs' tensor memory
+      asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                       smem_u32(&s_tmem)),
+                   "r"(S::TMEM_COLS));
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+    } else {
+      asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                       smem_u32(&s_tmem)),
+                   "r"(S::TMEM_COLS));
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
   }
   tc_fence_before();
   __syncthreads();
+  // CG = 2: both CTAs' barriers are initialised and the pair's tensor memory allocated before
+  // either CTA loads into, commits to or arrives on the other's barriers
+  if constexpr (CG == 2) cluster_sync();
   tc_fence_after();
   const uint32_t tmem = s_tmem;
   pdl_wait();
@@ -252,13 +315,20 @@ __global__ void __launch_bounds__(NT, 1)
       uint32_t issued = 0;  // bit s: stage s has a load in flight or landed (phase ph_of[s])
       uint32_t ph_of = 0;
       for (int t = t_first; t < tiles; t += t_step) {
-        const int m0 = (t % m_tiles) * BM, n0 = (t / m_tiles) * BN;
+        const int m0 = (t % m_tiles) * TM + mrow, n0 = (t / m_tiles) * BN + (int)rank * (BN / 2) * (CG - 1);
         for (int kb = 0; kb < nk; ++kb) {
           if (!mbar_wait(&empty[s], ph ^ 1, err, ERR_TIMEOUT_PRODUCER)) goto producer_done;
           uint8_t* st = sbase + s * S::STAGE;
-          mbar_expect_tx(&full[s], S::STAGE);
-          tma_load_2d(st, &tmA, &full[s], (kb0 + kb) * BK, m0);
-          tma_load_2d(st + S::A_BYTES, &tmB, &full[s], (kb0 + kb) * BK, n0);
+          if constexpr (CG == 2) {
+            if (leader) mbar_expect_tx(&full[s], 2 * S::STAGE);  // both CTAs' bytes
+            const uint32_t fb = map_rank(smem_u32(&full[s]), 0);
+            tma_load_2d_pair(st, &tmA, fb, (kb0 + kb) * BK, m0);
+            tma_load_2d_pair(st + S::A_BYTES, &tmB, fb, (kb0 + kb) * BK, n0);
+          } else {
+            mbar_expect_tx(&full[s], S::STAGE);
+            tma_load_2d(st, &tmA, &full[s], (kb0 + kb) * BK, m0);
+            tma_load_2d(st + S::A_BYTES, &tmB, &full[s], (kb0 + kb) * BK, n0);
+          }
           issued |= 1u << s;
           ph_of = (ph_of & ~(1u << s)) | (ph << s);
           if (++s == STAGES) {
@@ -268,14 +338,20 @@ __global__ void __launch_bounds__(NT, 1)
         }
       }
     producer_done:
-      // never leave with a TMA write into this CTA's shared memory still in flight
+      // never leave with a TMA write into this CTA's shared memory still in flight (the odd CTA
+      // of a pair: its loads complete on the even CTA's barrier, which the MMAs that read them
+      // wait for; their commit on this CTA's slot barrier says they have landed)
       for (int st = 0; st < STAGES; ++st)
-        if (issued & (1u << st))
-          mbar_wait(&full[st], (ph_of >> st) & 1u, err, ERR_TIMEOUT_PRODUCER, false);
+        if (issued & (1u << st)) {
+          if (leader)
+            mbar_wait(&full[st], (ph_of >> st) & 1u, err, ERR_TIMEOUT_PRODUCER, false);
+          else
+            mbar_wait(&empty[st], (ph_of >> st) & 1u, err, ERR_TIMEOUT_PRODUCER, false);
+        }
     }
   } else if (warp == 1) {
-    if (lane == 0) {  // MMA issuer
-      constexpr uint32_t idesc = idesc_f16<T>(BM, BN);
+    if (lane == 0 && leader) {  // MMA issuer
+      constexpr uint32_t idesc = idesc_f16<T>(TM, BN);
       int s = 0;
       uint32_t ph = 0;
       int i = 0;
@@ -290,20 +366,33 @@ __global__ void __launch_bounds__(NT, 1)
           tc_fence_after();
           const uint32_t sa = smem_u32(sbase + s * S::STAGE);
           const uint64_t da = desc_sw128(sa), db = desc_sw128(sa + S::A_BYTES);
+          if constexpr (CG == 2) {
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k)  // +32 B per K step inside the swizzle row
-            umma_f16(d, da + 2 * k, db + 2 * k, idesc, (kb | k) != 0);
-          umma_commit(&empty[s]);
+            for (int k = 0; k < BK / 16; ++k)
+              umma_f16_pair(d, da + 2 * k, db + 2 * k, idesc, (kb | k) != 0);
+            umma_commit_pair_both(&empty[s]);
+          } else {
+#pragma unroll
+            for (int k = 0; k < BK / 16; ++k)  // +32 B per K step inside the swizzle row
+              umma_f16(d, da + 2 * k, db + 2 * k, idesc, (kb | k) != 0);
+            umma_commit(&empty[s]);
+          }
           if (++s == STAGES) {
             s = 0;
             ph ^= 1;
           }
         }
-        umma_commit(&tfull[acc]);
+        if constexpr (CG == 2)
+          umma_commit_pair_both(&tfull[acc]);
+        else
+          umma_commit(&tfull[acc]);
       }
     mma_done:
       // every issued MMA completes before TMEM is released
-      umma_commit(&drain);
+      if constexpr (CG == 2)
+        umma_commit_pair(&drain);
+      else
+        umma_commit(&drain);
       mbar_wait(&drain, 0, err, ERR_TIMEOUT_MMA, false);
     }
   } else if (KS > 1) {  // split-K pair: park the peer's half of the accumulator
@@ -341,7 +430,7 @@ __global__ void __launch_bounds__(NT, 1)
     for (int t = t_first; t < tiles; t += t_step, ++i) {
       const int acc = i & 1;
       const uint32_t aph = (i >> 1) & 1;
-      const int m0 = (t % m_tiles) * BM, n0 = (t / m_tiles) * BN;
+      const int m0 = (t % m_tiles) * TM + mrow, n0 = (t / m_tiles) * BN;
       // request every global operand of this warp's chunks into L1 while the accumulator is
       // still being computed (the epilogue warps are otherwise idle then)
       {
@@ -374,7 +463,12 @@ __global__ void __launch_bounds__(NT, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[acc]);
+      if (lane == 0) {
+        if (leader)
+          mbar_arrive(&tempty[acc]);
+        else  // the even CTA's MMA issuer reuses the pair's accumulator
+          mbar_arrive_cluster(map_rank(smem_u32(&tempty[acc]), 0));
+      }
     }
   }
 
@@ -443,10 +537,17 @@ __global__ void __launch_bounds__(NT, 1)
 
   tc_fence_before();
   __syncthreads();
+  // CG = 2: the even CTA's MMAs (which read this CTA's shared memory and write its tensor
+  // memory) have completed and neither CTA arrives on the other's barriers any more
+  if constexpr (CG == 2) cluster_sync();
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
-                 "r"(S::TMEM_COLS));
+    if constexpr (CG == 2)
+      asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                   "r"(S::TMEM_COLS));
+    else
+      asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                   "r"(S::TMEM_COLS));
   }
 }
 

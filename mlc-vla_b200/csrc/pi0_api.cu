@@ -146,6 +146,7 @@ struct pi0_ctx {
   int num_sms = 148;
   bool use_tc = true;      // tensor-core (tcgen05) GEMMs for M >= 128
   bool pdl = true;         // programmatic dependent launch between the kernels of a chain
+  bool cta_pair = true;    // 256 × 256 CTA-pair tiles where they fill the SMs (PI0_CTA_PAIR=0: off)
 
   cudaStream_t cap_stream = nullptr;
   std::map<GraphKey, std::pair<cudaGraphExec_t, int64_t>> graphs;  // exec, kernel nodes
@@ -428,6 +429,31 @@ int gemm_tc_pair_launch(pi0_ctx* ctx, const T* A, int lda, const T* W, int ldw, 
                 tc::Smem<BN, ST>::BYTES, st, dim3(2, 1, 1), ta, tb, M, N, K, epi, ctx->dev_err);
 }
 
+// CTA-pair tiles (gemm_tc_kernel CG = 2): 256 × 256 output tiles on tcgen05 cta_group::2,
+// persistent pairs. For GEMMs with many 256-wide tiles (the prefill gate/up projection: 512 pair
+// tiles), where a single CTA's 128 × 256 tile is limited by how fast L2 refills its ring: each
+// CTA of a pair loads 128 rows of A and 128 rows of W per k-block instead of 128 + 256.
+constexpr int kPairST = 6;
+bool use_cta_pair(int M, int N, int sms) {
+  const int pairs = ((M + 255) / 256) * ((N + 255) / 256);
+  return M > 256 && N % 256 == 0 && pairs >= 2 * (sms / 2);
+}
+template <typename T, class Epi>
+int gemm_tc_cg2_launch(pi0_ctx* ctx, const T* A, int lda, const T* W, int ldw, int M, int N,
+                       int K, const Epi& epi, cudaStream_t st, int fam) {
+  constexpr int BN = 256;
+  CUtensorMap ta, tb;
+  const bool bf = Tr<T>::kBf16;
+  TRY(make_tmap(ctx, &ta, A, M, K, lda, tc::BM, bf));
+  TRY(make_tmap(ctx, &tb, W, N, K, ldw, BN / 2, bf));
+  const int pairs = ((M + 2 * tc::BM - 1) / (2 * tc::BM)) * ((N + BN - 1) / BN);
+  const int grid = 2 * std::min(pairs, ctx->num_sms / 2);
+  Prof pr(ctx, fam, st);
+  return launch(ctx, tc::gemm_tc_kernel<T, BN, kPairST, Epi, 1, 2>, dim3(grid), dim3(tc::NT),
+                tc::Smem<BN, kPairST, 2>::BYTES, st, dim3(2, 1, 1), ta, tb, M, N, K, epi,
+                ctx->dev_err);
+}
+
 template <typename T>
 int rmsnorm(pi0_ctx* ctx, const T* x, T* out, int rows, int W, const T* w, const T* mod,
             int rows_per_mod, int mod_stride, cudaStream_t st, int fam);
@@ -560,9 +586,12 @@ int gemm(pi0_ctx* ctx, const T* A, int lda, const T* W, int ldw, int M, int N, i
     if (M <= 64) return skinny_launch<T, 64, false, false>(ctx, A, lda, W, ldw, M, N, K, epi, st, fam, SkOpt{});
     return skinny_launch<T, 128, false, false>(ctx, A, lda, W, ldw, M, N, K, epi, st, fam, SkOpt{});
   }
+  if (engine == 5) return gemm_tc_cg2_launch<T>(ctx, A, lda, W, ldw, M, N, K, epi, st, fam);
   if ((engine == 0 && M >= 128 && ctx->use_tc) || engine == 1 || engine == 4) {
     if (engine == 4 || (engine == 0 && use_splitk_pair(M, N, K, ctx->num_sms)))
       return gemm_tc_pair_launch<T>(ctx, A, lda, W, ldw, M, N, K, epi, st, fam);
+    if (engine == 0 && ctx->cta_pair && use_cta_pair(M, N, ctx->num_sms))
+      return gemm_tc_cg2_launch<T>(ctx, A, lda, W, ldw, M, N, K, epi, st, fam);
     switch (pick_bn(M, N, ctx->num_sms)) {
       case 256: return gemm_tc_launch<T, 256, 4>(ctx, A, lda, W, ldw, M, N, K, epi, st, fam);
       case 160: return gemm_tc_launch<T, 160, 5>(ctx, A, lda, W, ldw, M, N, K, epi, st, fam);
@@ -1193,10 +1222,11 @@ int attr_gemm(pi0_ctx* ctx) {
                           GemmCfg<T, BM, BN, WM, WN, ST>::SMEM));
   return 0;
 }
-template <typename T, int BN, int ST, class Epi, int KS = 1>
+template <typename T, int BN, int ST, class Epi, int KS = 1, int CG = 1>
 int attr_tc(pi0_ctx* ctx) {
-  CK(cudaFuncSetAttribute(tc::gemm_tc_kernel<T, BN, ST, Epi, KS>,
-                          cudaFuncAttributeMaxDynamicSharedMemorySize, tc::Smem<BN, ST>::BYTES));
+  CK(cudaFuncSetAttribute(tc::gemm_tc_kernel<T, BN, ST, Epi, KS, CG>,
+                          cudaFuncAttributeMaxDynamicSharedMemorySize,
+                          tc::Smem<BN, ST, CG>::BYTES));
   return 0;
 }
 template <typename T, int NA, class Epi, bool SSQ = false>
@@ -1219,6 +1249,7 @@ int attr_gemm_both(pi0_ctx* ctx) {
   TRY((attr_tc<T, 256, 4, Epi, 2>(ctx)));
   TRY((attr_tc<T, 160, 5, Epi>(ctx)));
   TRY((attr_tc<T, 128, 6, Epi>(ctx)));
+  TRY((attr_tc<T, 256, kPairST, Epi, 1, 2>(ctx)));
   return 0;
 }
 template <typename T, int HD>
@@ -1738,6 +1769,7 @@ int pi0_create(const pi0_config* cfg, int device, pi0_ctx** out) {
   int sms = 0;
   CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
   ctx->num_sms = sms;
+  if (const char* env = std::getenv("PI0_CTA_PAIR")) ctx->cta_pair = env[0] != '0';
   CK(cudaStreamCreateWithFlags(&ctx->cap_stream, cudaStreamNonBlocking));
   TRY(alloc_all(ctx));
   TRY(is_bf16(ctx) ? setup_attrs<__nv_bfloat16>(ctx) : setup_attrs<__half>(ctx));
@@ -1966,6 +1998,7 @@ int pi0_linear(pi0_ctx* ctx, const void* x, int M, int K, const void* w, int N, 
   if (!ctx || !x || !w || !y || M < 1 || N < 2 || K < 8 || (N & 1) || (K % 8))
     return fail(ctx, PI0_ERR_INVALID, "pi0_linear: need M >= 1, even N, K a multiple of 8");
   if (engine == 2 && K % 32) return fail(ctx, PI0_ERR_INVALID, "warp-level engine needs K % 32 == 0");
+  if (engine < 0 || engine > 5) return fail(ctx, PI0_ERR_INVALID, "pi0_linear: engine must be 0..5");
   CK(cudaSetDevice(ctx->device));
   if (is_bf16(ctx)) {
     using T = __nv_bfloat16;

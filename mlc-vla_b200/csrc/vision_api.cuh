@@ -191,6 +191,7 @@ int attr_tc_all(pi0_ctx* ctx) {
   TRY((attr_tc<T, 160, 5, Epi>(ctx)));
   TRY((attr_tc<T, 128, 6, Epi>(ctx)));
   TRY((attr_tc<T, 128, 6, Epi, 2>(ctx)));
+  TRY((attr_tc<T, 256, kPairST, Epi, 1, 2>(ctx)));
   return 0;
 }
 
@@ -386,6 +387,7 @@ int pi0_vision_create(const pi0_vision_config* cfg, int device, pi0_vision_ctx**
   int sms = 0;
   CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
   ctx->num_sms = sms;
+  if (const char* env = std::getenv("PI0_CTA_PAIR")) ctx->cta_pair = env[0] != '0';
   CK(cudaStreamCreateWithFlags(&ctx->cap_stream, cudaStreamNonBlocking));
   TRY(vision_alloc(v));
   return cfg->dtype == PI0_BF16 ? vision_attrs<__nv_bfloat16>(v) : vision_attrs<__half>(v);

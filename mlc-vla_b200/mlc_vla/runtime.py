@@ -329,7 +329,8 @@ class Pi0Runtime:
 
     def linear(self, x: torch.Tensor, w: torch.Tensor, engine: int = 0) -> torch.Tensor:
         """y = x·wᵀ on the library's GEMM engine (0 auto, 1 tcgen05 tiles, 2 warp-level mma,
-        3 weight-streaming split-K, 4 tcgen05 tiles split over K between a CTA pair)."""
+        3 weight-streaming split-K, 4 tcgen05 tiles split over K between a CTA pair, 5 tcgen05
+        256×256 tiles on a CTA pair with cta_group::2 MMAs)."""
         x = self._t(x, self.dtype)
         w = self._t(w, self.dtype)
         m, k = x.shape

@@ -16,7 +16,7 @@ def rt():
     return Pi0Runtime(config(recipes.MINI), device=0)
 
 
-@pytest.mark.parametrize("engine", [1, 2, 3, 4])
+@pytest.mark.parametrize("engine", [1, 2, 3, 4, 5])
 @pytest.mark.parametrize("m,n,k", [(128, 256, 64), (968, 2560, 2048), (200, 160, 320),
                                    (50, 1024, 4096), (777, 390, 96), (1000, 32768, 128),
                                    (50, 2560, 1024), (50, 8192, 1024), (50, 1024, 2048),
@@ -31,6 +31,8 @@ def test_linear_matches_torch_fp32(rt, engine, m, n, k):
         pytest.skip("tile engine: M >= 128")
     if engine == 4 and (m < 128 or k <= 64):
         pytest.skip("split-K pair engine: M >= 128, K > 64")
+    if engine == 5 and m < 128:
+        pytest.skip("CTA-pair tile engine: M >= 128")
     g = torch.Generator(device="cuda").manual_seed(m * 7 + n + k)
     x = torch.randn((m, k), generator=g, device="cuda").half()
     w = (0.05 * torch.randn((n, k), generator=g, device="cuda")).half()
@@ -43,3 +45,26 @@ def test_linear_matches_torch_fp32(rt, engine, m, n, k):
     assert err.max().item() <= tol, (err.max().item(), tol)
     rel = (err.norm() / ref.norm()).item()
     assert rel < 2e-3
+
+
+@pytest.mark.parametrize("m,n,k", [(968, 32768, 2048), (200, 512, 192), (1000, 1280, 4160)])
+def test_cta_pair_tiles_equal_single_cta_tiles(rt, m, n, k):
+    """A 256-row tile on a CTA pair (cta_group::2) accumulates every output over K in the same
+    order as a 128-row tile on one CTA: the two engines give the same bits."""
+    g = torch.Generator(device="cuda").manual_seed(m + 3 * n + k)
+    x = torch.randn((m, k), generator=g, device="cuda").half()
+    w = (0.05 * torch.randn((n, k), generator=g, device="cuda")).half()
+    y1 = rt.linear(x, w, engine=1)
+    y5 = rt.linear(x, w, engine=5)
+    torch.cuda.synchronize()
+    assert rt.device_error() == 0
+    assert torch.equal(y1, y5), (y1.float() - y5.float()).abs().max().item()
+
+
+def test_engine_number_out_of_range_is_refused(rt):
+    from mlc_vla import _lib
+
+    x = torch.zeros((128, 64), dtype=torch.float16, device="cuda")
+    w = torch.zeros((64, 64), dtype=torch.float16, device="cuda")
+    with pytest.raises(_lib.Pi0Error):
+        rt.linear(x, w, engine=6)
