@@ -9,7 +9,9 @@
 //   * the accumulator is double buffered in TMEM (2·BN columns), so eight epilogue warps drain
 //     tile i (tcgen05.ld → registers → functor) while the MMA warp accumulates tile i+1;
 //   * persistent CTAs (one per SM) walk the tiles M-fastest, so the CTAs working at the same
-//     time share W tiles through L2 and every weight byte comes from HBM about once.
+//     time share W tiles through L2 and every weight byte comes from HBM about once;
+//   * two cluster modes: a K split between two CTAs (KS = 2) for long-K GEMMs of few tiles, and
+//     256-row tiles on a CTA pair with tcgen05 cta_group::2 (CG = 2) for GEMMs of many tiles.
 // Every mbarrier wait is bounded (about one second of globaltimer); on timeout the kernel sets
 // *err, leaves its loops, waits for its own tensor-core work and frees TMEM before returning.
 #pragma once

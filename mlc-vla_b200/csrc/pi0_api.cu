@@ -146,7 +146,7 @@ struct pi0_ctx {
   int num_sms = 148;
   bool use_tc = true;      // tensor-core (tcgen05) GEMMs for M >= 128
   bool pdl = true;         // programmatic dependent launch between the kernels of a chain
-  bool cta_pair = true;    // 256 × 256 CTA-pair tiles where they fill the SMs (PI0_CTA_PAIR=0: off)
+  bool cta_pair = true;    // CTA-pair tiles for GEMMs of two or more waves (PI0_CTA_PAIR=0: off)
 
   cudaStream_t cap_stream = nullptr;
   std::map<GraphKey, std::pair<cudaGraphExec_t, int64_t>> graphs;  // exec, kernel nodes
@@ -430,18 +430,20 @@ int gemm_tc_pair_launch(pi0_ctx* ctx, const T* A, int lda, const T* W, int ldw, 
 }
 
 // CTA-pair tiles (gemm_tc_kernel CG = 2): 256 × 256 output tiles on tcgen05 cta_group::2,
-// persistent pairs. For GEMMs with many 256-wide tiles (the prefill gate/up projection: 512 pair
-// tiles), where a single CTA's 128 × 256 tile is limited by how fast L2 refills its ring: each
-// CTA of a pair loads 128 rows of A and 128 rows of W per k-block instead of 128 + 256.
-constexpr int kPairST = 6;
+// persistent pairs; each CTA of a pair loads 128 rows of A and 128 rows of W per k-block
+// instead of 128 + 256. Used where the pair tiles fill the SMs at least twice over (the prefill
+// gate/up projection: 512 pair tiles at batch 1; every prefill projection at batch 8), so each
+// pair streams several tiles through a full ring. On GEMMs of one wave (the batch-1 q/k/v and
+// o projections, the vision projections) they measured 5-20 % slower than single-CTA tiles.
+template <int BN> constexpr int pair_stages() { return BN == 256 ? 6 : 8; }
 bool use_cta_pair(int M, int N, int sms) {
   const int pairs = ((M + 255) / 256) * ((N + 255) / 256);
   return M > 256 && N % 256 == 0 && pairs >= 2 * (sms / 2);
 }
-template <typename T, class Epi>
+template <typename T, int BN, class Epi>
 int gemm_tc_cg2_launch(pi0_ctx* ctx, const T* A, int lda, const T* W, int ldw, int M, int N,
                        int K, const Epi& epi, cudaStream_t st, int fam) {
-  constexpr int BN = 256;
+  constexpr int ST = pair_stages<BN>();
   CUtensorMap ta, tb;
   const bool bf = Tr<T>::kBf16;
   TRY(make_tmap(ctx, &ta, A, M, K, lda, tc::BM, bf));
@@ -449,8 +451,8 @@ int gemm_tc_cg2_launch(pi0_ctx* ctx, const T* A, int lda, const T* W, int ldw, i
   const int pairs = ((M + 2 * tc::BM - 1) / (2 * tc::BM)) * ((N + BN - 1) / BN);
   const int grid = 2 * std::min(pairs, ctx->num_sms / 2);
   Prof pr(ctx, fam, st);
-  return launch(ctx, tc::gemm_tc_kernel<T, BN, kPairST, Epi, 1, 2>, dim3(grid), dim3(tc::NT),
-                tc::Smem<BN, kPairST, 2>::BYTES, st, dim3(2, 1, 1), ta, tb, M, N, K, epi,
+  return launch(ctx, tc::gemm_tc_kernel<T, BN, ST, Epi, 1, 2>, dim3(grid), dim3(tc::NT),
+                tc::Smem<BN, ST, 2>::BYTES, st, dim3(2, 1, 1), ta, tb, M, N, K, epi,
                 ctx->dev_err);
 }
 
@@ -586,12 +588,12 @@ int gemm(pi0_ctx* ctx, const T* A, int lda, const T* W, int ldw, int M, int N, i
     if (M <= 64) return skinny_launch<T, 64, false, false>(ctx, A, lda, W, ldw, M, N, K, epi, st, fam, SkOpt{});
     return skinny_launch<T, 128, false, false>(ctx, A, lda, W, ldw, M, N, K, epi, st, fam, SkOpt{});
   }
-  if (engine == 5) return gemm_tc_cg2_launch<T>(ctx, A, lda, W, ldw, M, N, K, epi, st, fam);
+  if (engine == 5) return gemm_tc_cg2_launch<T, 256>(ctx, A, lda, W, ldw, M, N, K, epi, st, fam);
   if ((engine == 0 && M >= 128 && ctx->use_tc) || engine == 1 || engine == 4) {
     if (engine == 4 || (engine == 0 && use_splitk_pair(M, N, K, ctx->num_sms)))
       return gemm_tc_pair_launch<T>(ctx, A, lda, W, ldw, M, N, K, epi, st, fam);
     if (engine == 0 && ctx->cta_pair && use_cta_pair(M, N, ctx->num_sms))
-      return gemm_tc_cg2_launch<T>(ctx, A, lda, W, ldw, M, N, K, epi, st, fam);
+      return gemm_tc_cg2_launch<T, 256>(ctx, A, lda, W, ldw, M, N, K, epi, st, fam);
     switch (pick_bn(M, N, ctx->num_sms)) {
       case 256: return gemm_tc_launch<T, 256, 4>(ctx, A, lda, W, ldw, M, N, K, epi, st, fam);
       case 160: return gemm_tc_launch<T, 160, 5>(ctx, A, lda, W, ldw, M, N, K, epi, st, fam);
@@ -1249,7 +1251,7 @@ int attr_gemm_both(pi0_ctx* ctx) {
   TRY((attr_tc<T, 256, 4, Epi, 2>(ctx)));
   TRY((attr_tc<T, 160, 5, Epi>(ctx)));
   TRY((attr_tc<T, 128, 6, Epi>(ctx)));
-  TRY((attr_tc<T, 256, kPairST, Epi, 1, 2>(ctx)));
+  TRY((attr_tc<T, 256, pair_stages<256>(), Epi, 1, 2>(ctx)));
   return 0;
 }
 template <typename T, int HD>

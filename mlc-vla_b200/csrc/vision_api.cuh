@@ -191,7 +191,7 @@ int attr_tc_all(pi0_ctx* ctx) {
   TRY((attr_tc<T, 160, 5, Epi>(ctx)));
   TRY((attr_tc<T, 128, 6, Epi>(ctx)));
   TRY((attr_tc<T, 128, 6, Epi, 2>(ctx)));
-  TRY((attr_tc<T, 256, kPairST, Epi, 1, 2>(ctx)));
+  TRY((attr_tc<T, 256, pair_stages<256>(), Epi, 1, 2>(ctx)));
   return 0;
 }
 
