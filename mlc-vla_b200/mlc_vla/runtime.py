@@ -68,8 +68,11 @@ class DeviceArray:
         return f"DeviceArray(shape={self.shape}, dtype={self.dtype}, device={self.torch.device})"
 
 
-def to_device(x, dtype: str, device) -> torch.Tensor:
-    """numpy / torch / DeviceArray -> contiguous torch tensor of `dtype` on `device`."""
+def to_device(x, dtype: str, device, non_blocking: bool = False) -> torch.Tensor:
+    """numpy / torch / DeviceArray -> contiguous torch tensor of `dtype` on `device`.
+
+    `non_blocking`: a pinned host tensor is copied on the current stream without waiting for the
+    copy; the caller must not reuse the host memory until it synchronises with that stream."""
     if isinstance(x, DeviceArray):
         x = x.torch
     if isinstance(x, torch.Tensor):
@@ -81,7 +84,8 @@ def to_device(x, dtype: str, device) -> torch.Tensor:
         if a.dtype == np.uint32:  # packed quantisation codes: keep the bits (int32 storage)
             a = a.view(np.int32)
         t = torch.from_numpy(np.ascontiguousarray(a))
-    return t.to(device=device, dtype=TORCH_DTYPE[dtype]).contiguous()
+    nb = non_blocking and t.device.type == "cpu" and t.is_pinned()
+    return t.to(device=device, dtype=TORCH_DTYPE[dtype], non_blocking=nb).contiguous()
 
 
 def config_struct(cfg: Pi0Config, max_batch: int = 1, quant=None) -> _lib.Pi0ConfigC:

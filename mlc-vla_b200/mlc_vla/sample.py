@@ -122,7 +122,9 @@ class PiZeroRunner:
         prefix_mask, suffix_cos, suffix_sin, nvs = self._pad_tables(pads)
         dev = self.dev
         x = prefix_embs if isinstance(prefix_embs, torch.Tensor) else np.asarray(prefix_embs)
-        prefix_dev = to_device(x, self._dt(), dev)
+        # a pinned host prefix goes up without the host waiting for the copy (every caller of
+        # _prepare reads its result back before returning, so the host buffer is free by then)
+        prefix_dev = to_device(x, self._dt(), dev, non_blocking=True)
         st = self._staging(b)
         k, v = self.ex.prefill(prefix_dev, prefix_mask, params, keys=st["keys"], values=st["values"])
         keys, values = DeviceArray(k), DeviceArray(v)
@@ -206,11 +208,18 @@ class PiZeroRunner:
         b = self._batch(prefix_embs)
         noise = self._noise(noise, seed, b)
         st = self._staging(b)
-        st["x0"].copy_(torch.from_numpy(noise.reshape(st["x0"].shape)), non_blocking=False)
-        st["pmask"].copy_(pmask.torch if isinstance(pmask, DeviceArray) else pmask)
-        st["scos"].copy_(scos)
-        st["ssin"].copy_(ssin)
-        st["te"].copy_(self._time_table(n))
+        # the noise goes up from a pinned staging buffer without a host wait (a pageable copy
+        # would hold the host until the prefill has run, leaving the GPU idle while the loop is
+        # launched); the previous call's copies finished before it returned
+        st["x0_host"].copy_(torch.from_numpy(noise.reshape(st["x0"].shape)))
+        st["x0"].copy_(st["x0_host"], non_blocking=True)
+        # the loop's graph reads fixed buffers: refresh them only when the cached tables change
+        src = (pmask.torch if isinstance(pmask, DeviceArray) else pmask, scos, ssin,
+               self._time_table(n))
+        if st.get("src") is None or any(old is not new for old, new in zip(st["src"], src)):
+            for name, t in zip(("pmask", "scos", "ssin", "te"), src):
+                st[name].copy_(t)
+            st["src"] = src
         self.ex.denoise_loop_kv(keys.torch, values.torch, st["x0"], st["te"], st["scos"],
                                 st["ssin"], st["pmask"], params, out=st["x"])
         return st["x"].cpu().numpy()
@@ -228,6 +237,8 @@ class PiZeroRunner:
                 "keys": torch.empty(kv, dtype=torch.float32, device=dev),
                 "values": torch.empty(kv, dtype=tdt, device=dev),
                 "x0": torch.empty((b, cfg.action_horizon, cfg.action_dim), dtype=torch.float32, device=dev),
+                "x0_host": torch.empty((b, cfg.action_horizon, cfg.action_dim), dtype=torch.float32,
+                                       pin_memory=True),
                 "x": torch.empty((b, cfg.action_horizon, cfg.action_dim), dtype=torch.float32, device=dev),
                 "te": torch.empty((cfg.num_denoise_steps, cfg.action_expert.width), dtype=tdt, device=dev),
                 "pmask": torch.empty((b, 1, 1, cfg.prefix_len), dtype=torch.float32, device=dev),
