@@ -117,3 +117,30 @@ def test_cached_tables_follow_the_pad_pattern(runner, loaded):
     fparams = fresh.to_params(list(params))
     assert np.array_equal(fresh.sample_graph(fparams, prefix, noise=noise, prefix_pad=pad_b),
                           outs[1])
+
+
+def test_sample_graph_from_pinned_host_buffers(runner, loaded):
+    """The pinned-prefix upload and the staged noise upload are asynchronous: results equal the
+    device-resident call bit for bit, a pinned buffer rewritten right after a call returns does
+    not leak into that call, and the table buffers follow a change of pad pattern."""
+    import torch
+
+    params, prefix = loaded
+    cfg = runner.config
+    rng = np.random.default_rng(11)
+    noises = [rng.standard_normal((1, cfg.action_horizon, cfg.action_dim)).astype("float32")
+              for _ in range(2)]
+    prefixes = [prefix, (prefix + 0.01 * rng.standard_normal(prefix.shape)).astype("float32")]
+    want = [runner.sample_graph(params, torch.from_numpy(p).cuda(), noise=n)
+            for p, n in zip(prefixes, noises)]
+    pinned = torch.from_numpy(prefixes[0].copy()).pin_memory()
+    for i in range(2):
+        got = runner.sample_graph(params, pinned, noise=noises[i])
+        np.testing.assert_array_equal(got, want[i])
+        pinned.copy_(torch.from_numpy(prefixes[1]))  # next call's prefix, written at once
+    pad = np.ones((cfg.prefix_len,), np.float32)
+    pad[-3:] = 0
+    padded = runner.sample_graph(params, pinned, noise=noises[1], prefix_pad=pad)
+    again = runner.sample_graph(params, pinned, noise=noises[1])
+    np.testing.assert_array_equal(again, want[1])
+    assert not np.array_equal(padded, want[1])
