@@ -68,3 +68,28 @@ def test_engine_number_out_of_range_is_refused(rt):
     w = torch.zeros((64, 64), dtype=torch.float16, device="cuda")
     with pytest.raises(_lib.Pi0Error):
         rt.linear(x, w, engine=6)
+
+
+def test_cta_pair_tiles_bf16():
+    """The CTA-pair engine in a bfloat16 context (the MMA's operand type bits): equal to the
+    single-CTA tiles bit for bit and within rounding of a torch fp32 product, at the prefill
+    gate/up shape the automatic choice sends to it."""
+    from gpu_common import config
+    from mlc_vla.runtime import Pi0Runtime
+    from tests.golden import recipes
+
+    rt = Pi0Runtime(config(recipes.MINI, "bfloat16"), device=0)
+    m, n, k = 968, 32768, 2048
+    g = torch.Generator(device="cuda").manual_seed(5)
+    x = torch.randn((m, k), generator=g, device="cuda").bfloat16()
+    w = (0.05 * torch.randn((n, k), generator=g, device="cuda")).bfloat16()
+    y1 = rt.linear(x, w, engine=1)
+    y5 = rt.linear(x, w, engine=5)
+    y0 = rt.linear(x, w, engine=0)
+    torch.cuda.synchronize()
+    assert rt.device_error() == 0
+    assert torch.equal(y1, y5) and torch.equal(y0, y5)
+    ref = x.float() @ w.float().T
+    rel = ((y5.float() - ref).norm() / ref.norm()).item()
+    assert rel < 4e-3, rel
+    rt.close()
